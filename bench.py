@@ -1,0 +1,466 @@
+"""Benchmark: KAT_Group forward+backward throughput (Gelem/s) on B200, one process per GPU.
+
+Workload (default): KAT_Group bf16 at the ViT-B MLP-hidden shape x[128,197,3072] ~ N(0,1),
+num_groups=8, 'gelu' coefficients + N(0, 0.01) perturbation, grad_out ~ N(0,1) — the
+configuration the headline metric is quoted on.  A step is one forward and one backward
+pass of the module over that batch (y = mod(x); y.backward(gy)); with N GPUs every rank
+processes its own batch (weak scaling) and the coefficient gradients are all-gathered over
+NCCL and summed in rank order each step.
+
+Printed (rank 0, one JSON line):
+  value        whole-job Gelem/s with inputs resident in HBM (device-timed, CUDA events,
+               max over ranks); each tensor (155 MB) is larger than the 126 MB L2
+  e2e          the same step through the module with host buffers: pinned-host -> device
+               copies of x and grad_out, forward+backward, device -> host copies of y, dx
+               and the coefficient gradients, all inside the timed region
+  roofline     the dominant kernel (the fused backward: read x, grad_out; write dx) against
+               the measured HBM copy bandwidth in MEASURED_PEAKS.json
+  cpu_baseline the reference's CPU path (the oracle's restatement of kat_1dgroup_torch.py,
+               fp32 upcast) on a bounded sample of the same workload, on this host's cores
+  clocks       SM clocks sampled with nvidia-smi while the GPU was busy
+
+`--impl reference` times only the reference's CPU implementation (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+METRIC = "KAT_Group fwd+bwd Gelem/s"
+UNIT = "Gelem/s"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="kat_group_vitb_bf16")
+    ap.add_argument("--no-graph", action="store_true", help="eager steps instead of a CUDA graph")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--kernel-iters", type=int, default=50)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="CPU budget of the reference-path baseline")
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_process_group(world, rank, local):
+    import datetime
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (nvidia-smi while the GPU works)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("uuid,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.uuid = None
+        try:
+            u = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.uuid = u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            pass
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            if self.uuid and parts[0] != self.uuid:
+                continue
+            self.samples.append(parts[1:])
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        rows = [[num(s[0]), num(s[1]), num(s[2]), num(s[3])] + s[4:] for s in self.samples]
+        busy = [r for r in rows if r[2] is not None and r[2] > 0 and r[0] is not None]
+        use = busy if busy else [r for r in rows if r[0] is not None]
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"],
+                    "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in use for i, v in enumerate(r[4:8])
+                          if str(v).strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in use),
+                "sm_max_mhz": max((r[1] for r in use if r[1] is not None), default=None),
+                "reasons": reasons, "samples": len(use),
+                "power_w_max": max((r[3] for r in use if r[3] is not None), default=None)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path (oracle restatement) on a bounded sample
+# ---------------------------------------------------------------------------
+
+def cpu_reference_rate(workload, budget_s: float, steps: int = 0, warmup: int = 0):
+    """Time fwd+bwd of the reference's PyTorch CPU path (restated in oracle/) on a sample of
+    `workload` rows.  Returns (Gelem/s, dict describing the sample)."""
+    from oracle import kat_torch_oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    wn, wd = workload.coefficients()
+    shape = list(workload.shape)
+    row_elems = workload.numel // shape[0]
+
+    def make(rows):
+        s = [rows] + shape[1:]
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(*s, generator=g).to(torch.bfloat16 if workload.dtype == "bf16" else
+                                            torch.float32 if workload.dtype == "f32" else
+                                            torch.float16).float()
+        gy = torch.randn(*s, generator=g).to(x.dtype)
+        return x, gy
+
+    def one(x, gy):
+        kat_torch_oracle.forward_backward(x, wn, wd, workload.groups, gy,
+                                          layout="nchw" if workload.layout == "nchw" else "blc")
+
+    # calibrate on one row
+    x, gy = make(1)
+    one(x, gy)
+    t0 = time.perf_counter()
+    one(x, gy)
+    per_row = max(time.perf_counter() - t0, 1e-4)
+    n_calls = (steps + warmup) if steps else 3
+    rows = int(max(1, min(shape[0], budget_s / max(n_calls, 1) / per_row)))
+    x, gy = make(rows)
+    for _ in range(warmup if steps else 1):
+        one(x, gy)
+    reps = steps if steps else 2
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one(x, gy)
+    dt = (time.perf_counter() - t0) / reps
+    elems = rows * row_elems
+    return elems / dt / 1e9, {
+        "cores": cores, "rows": rows, "elements": elems, "seconds_per_step": dt, "reps": reps,
+        "sample": f"x[{rows},{','.join(str(s) for s in shape[1:])}] of {workload.name} "
+                  f"(fp32 upcast), fwd+bwd, mean of {reps} timed steps"}
+
+
+def run_reference(args):
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    from rational_kat_cu_b200 import workloads
+
+    w = workloads.BY_NAME[args.workload]()
+    rate, info = cpu_reference_rate(w, budget_s=min(150.0, 10.0 + 0.5 * (args.steps + args.warmup)),
+                                    steps=args.steps, warmup=args.warmup)
+    line = {
+        "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": info["seconds_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": w.name, "shape": list(w.shape), "num_groups": w.groups,
+                   "sample_shape": [info["rows"]] + list(w.shape[1:])},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def run_ours(args):
+    import rational_kat_cu_b200 as kat
+    from rational_kat_cu_b200 import distributed as kdist
+    from rational_kat_cu_b200 import workloads
+
+    world, rank, local = dist_setup()
+    dist = init_process_group(world, rank, local) if world > 1 else None
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    w = workloads.BY_NAME[args.workload]()
+    w.x_seed += 1000 * rank
+    w.gy_seed += 1000 * rank
+    elem_bytes = {"f32": 4, "bf16": 2, "f16": 2}[w.dtype]
+    N = w.numel
+
+    wn, wd = w.coefficients()
+    cls = kat.KAT_Group2D if w.layout == "nchw" else kat.KAT_Group
+    mod = cls(num_groups=w.groups, mode="gelu").to(dev)
+    with torch.no_grad():
+        mod.weight_numerator.copy_(wn)
+        mod.weight_denominator.copy_(wd)
+    x, gy = w.inputs(dev)
+    x.requires_grad_(True)
+    stream = torch.cuda.current_stream(dev)
+
+    def step_eager():
+        y = mod(x)
+        y.backward(gy)
+        return y
+
+    # Warm up (also fills the workspace-size cache before any capture).
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            mod.zero_grad(set_to_none=True)
+            x.grad = None
+            step_eager()
+    stream.wait_stream(side)
+    torch.cuda.synchronize(dev)
+
+    graph = None
+    if not args.no_graph:
+        mod.zero_grad(set_to_none=True)
+        x.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step_eager()
+        torch.cuda.synchronize(dev)
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            mod.zero_grad(set_to_none=True)
+            x.grad = None
+            step_eager()
+        if dist is not None:
+            kdist.allreduce_coefficient_grads(mod)
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+
+    for _ in range(args.warmup):
+        step()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms_total], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_per_step = ms_total / args.steps
+    value = world * N / (ms_per_step * 1e-3) / 1e9
+
+    # Kernel-level timing of the forward and the fused backward (C ABI calls, device-resident
+    # inputs), per launch with CUDA events on the launching stream.
+    n_rep = wn.repeat(w.groups, 1).to(dev)
+    d_rep = wd.to(dev)
+    xs = x.detach()
+    fwd_fn = kat.rational_fwd_cuda_2d if w.layout == "nchw" else kat.rational_fwd_cuda
+    bwd_fn = kat.rational_bwd_cuda_2d if w.layout == "nchw" else kat.rational_bwd_cuda
+
+    def time_launches(fn, iters):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(iters)]
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        for a, b in evs:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    fwd_ms = time_launches(lambda: fwd_fn(xs, n_rep, d_rep, w.groups), args.kernel_iters)
+    bwd_ms = time_launches(lambda: bwd_fn(gy, xs, n_rep, d_rep, w.groups), args.kernel_iters)
+    fwd_gbs = 2 * N * elem_bytes / (fwd_ms * 1e-3) / 1e9
+    bwd_gbs = 3 * N * elem_bytes / (bwd_ms * 1e-3) / 1e9
+
+    # End to end through the module with host buffers.
+    h_x = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
+    h_gy = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
+    h_x.copy_(xs.cpu())
+    h_gy.copy_(gy.cpu())
+    h_y = torch.empty_like(h_x, pin_memory=True)
+    h_dx = torch.empty_like(h_x, pin_memory=True)
+    h_dn = torch.empty(mod.weight_numerator.shape, pin_memory=True)
+    h_dd = torch.empty(mod.weight_denominator.shape, pin_memory=True)
+
+    def e2e_step():
+        xd = h_x.to(dev, non_blocking=True).requires_grad_(True)
+        gd = h_gy.to(dev, non_blocking=True)
+        mod.zero_grad(set_to_none=True)
+        y = mod(xd)
+        y.backward(gd)
+        if dist is not None:
+            kdist.allreduce_coefficient_grads(mod)
+        h_y.copy_(y.detach(), non_blocking=True)
+        h_dx.copy_(xd.grad, non_blocking=True)
+        h_dn.copy_(mod.weight_numerator.grad, non_blocking=True)
+        h_dd.copy_(mod.weight_denominator.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = e_start.elapsed_time(e_end)
+    if dist is not None:
+        t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_ms_step = e_ms / args.e2e_steps
+    e2e_value = world * N / (e2e_ms_step * 1e-3) / 1e9
+    h2d = 2 * N * elem_bytes
+    d2h = 2 * N * elem_bytes + (h_dn.numel() + h_dd.numel()) * 4
+
+    clocks = None
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        rate, info = cpu_reference_rate(w, budget_s=args.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
+               "sample": info["sample"]}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        step_bytes = 5 * N * elem_bytes
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": w.dtype, "data": "synthetic",
+            "config": {
+                "workload": w.name, "shape": list(w.shape), "num_groups": w.groups,
+                "coefficients": "gelu + N(0,0.01)" if w.perturb else w.mode,
+                "elements_per_gpu": N, "layout": w.layout,
+                "l2": f"inputs larger than L2 ({N * elem_bytes / 1e6:.0f} MB per tensor > "
+                      f"{L2_BYTES / 1e6:.0f} MB)",
+                "step": "module forward + backward" + (" in a CUDA graph" if graph else "")
+                        + (" + NCCL coefficient-gradient all-gather" if world > 1 else ""),
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "kat_bwd_kernel (+ kat_bwd_reduce_kernel)",
+                "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
+                "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "algorithmic_bytes_per_launch": 3 * N * elem_bytes,
+                "ms_per_launch": bwd_ms,
+            },
+            "kernels": {
+                "fwd_ms": fwd_ms, "fwd_GBps": fwd_gbs, "fwd_frac": fwd_gbs / peak,
+                "bwd_ms": bwd_ms, "bwd_GBps": bwd_gbs, "bwd_frac": bwd_gbs / peak,
+                "step_hbm_frac": step_bytes * world / (ms_per_step * 1e-3) / 1e9 / (peak * world),
+            },
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms_step},
+            "gpu_launches": 3 * args.steps * world,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,147 @@
+/*
+ * kat_rational.h — C ABI of the B200 (sm_100a) group-rational activation library
+ * (libkat_rational.so).
+ *
+ * The activation is KAT's group rational function, evaluated exactly as the
+ * reference's PyTorch path does (kat_rational/kat_1dgroup_torch.py:27-78):
+ *
+ *     y = P(x) / Q(x),   P(x) = a0 + a1 x + a2 x^2 + a3 x^3 + a4 x^4 + a5 x^5
+ *                        Q(x) = 1 + |b1| x + |b2| x^2 + |b3| x^3 + |b4| x^4
+ *
+ * with one coefficient set (a[g,0..5], b[g,0..3]) per channel group g.  The
+ * absolute value is taken on the denominator coefficients only; the powers of x
+ * are raw (kat_1dgroup_torch.py:63-69), so Q can reach zero for x < 0.
+ *
+ * Tensor layout.  Every data tensor is contiguous and viewed as
+ * [batch, channels, inner]:
+ *   - channels-last input [B, L, C] or [B, C]  -> batch = B*L (or B), inner = 1
+ *   - NCHW input [B, C, H, W]                  -> batch = B,   inner = H*W
+ * Channel c belongs to group c / (channels / num_groups).
+ *
+ * Conventions.
+ *   - The caller owns every buffer (inputs, outputs and the backward workspace).
+ *     The library allocates no device memory, never synchronises the host and
+ *     enqueues work only on the given stream (a cudaStream_t passed as void*;
+ *     NULL = the legacy default stream) of the current CUDA device.
+ *   - Coefficients are fp32: numerator [num_groups, 6], denominator [num_groups, 4].
+ *   - Data tensors (x, y, grad_out, grad_x) share one dtype (KAT_DTYPE_*); all
+ *     arithmetic is fp32 and a 16-bit output is rounded once, to nearest even.
+ *   - Pointers of any alignment are accepted; 16-byte-aligned tensors whose group
+ *     width is a multiple of the vector width take the 128-bit vector path.
+ *   - Every entry point returns KAT_OK (0) or a KAT_ERR_* code; kat_rational_strerror()
+ *     describes it.  Argument errors are detected before anything is enqueued.
+ *   - Coefficient gradients are reduced in a fixed order (per-thread fp32 sums,
+ *     then fp64 per-block and grid sums, no floating-point atomics): for a given
+ *     shape, dtype and GPU model the results are bit-identical run to run.
+ */
+#ifndef KAT_RATIONAL_H_
+#define KAT_RATIONAL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KAT_RATIONAL_ABI_VERSION 1
+
+/* Data-tensor element types. */
+#define KAT_DTYPE_F32 0
+#define KAT_DTYPE_F16 1
+#define KAT_DTYPE_BF16 2
+
+/* Status codes. */
+#define KAT_OK 0
+#define KAT_ERR_NULL_POINTER 1      /* a required pointer is NULL */
+#define KAT_ERR_BAD_DTYPE 2         /* dtype is not one of KAT_DTYPE_* */
+#define KAT_ERR_BAD_SHAPE 3         /* negative extent, or size overflow */
+#define KAT_ERR_BAD_GROUPS 4        /* num_groups < 1 or channels % num_groups != 0 */
+#define KAT_ERR_WORKSPACE 5         /* workspace NULL or smaller than required */
+#define KAT_ERR_CUDA 6              /* CUDA runtime / launch error */
+
+/*
+ * Forward: y = P(x)/Q(x).
+ * Replaces the reference's forward launchers
+ *   kat_rational/rational_triton.py:76-94   (rational_fwd_triton, [B,L,C] / [B,C])
+ *   kat_rational/rational_triton2d.py:71-91 (rational_fwd_triton_2d, [B,C,H,W])
+ * with the formula of kat_rational/kat_1dgroup_torch.py:27-78.
+ */
+int kat_rational_fwd(const void* x, void* y,
+                     const float* numerator,    /* [num_groups, 6] */
+                     const float* denominator,  /* [num_groups, 4] */
+                     int64_t batch, int64_t channels, int64_t inner,
+                     int64_t num_groups, int dtype, void* stream);
+
+/*
+ * Backward: grad_x = dy/dx * grad_out, and the coefficient gradients
+ *   grad_numerator[g,k]   = sum over group g of grad_out * x^k / Q
+ *   grad_denominator[g,i] = sgn(b[g,i]) * sum over group g of -grad_out * P * x^(i+1) / Q^2
+ * (sgn(0) = 0, as torch's abs backward).  Both coefficient gradients are fully
+ * overwritten (no accumulation into existing values).  grad_x may be NULL, in
+ * which case only the coefficient gradients are produced.
+ * `workspace` must hold at least kat_rational_bwd_workspace_size() bytes and be
+ * 16-byte aligned; its contents on entry are irrelevant.
+ * Replaces kat_rational/rational_triton.py:217-238 (rational_bwd_triton) and
+ * kat_rational/rational_triton2d.py:194-220 (rational_bwd_triton_2d); the
+ * gradients are those torch autograd derives for kat_1dgroup_torch.py:27-78.
+ * Launches two kernels on `stream`: the fused elementwise/partial-sum kernel and
+ * the fixed-order grid reduction.
+ */
+int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x,
+                     const float* numerator, const float* denominator,
+                     float* grad_numerator,     /* [num_groups, 6] */
+                     float* grad_denominator,   /* [num_groups, 4] */
+                     void* workspace, size_t workspace_bytes,
+                     int64_t batch, int64_t channels, int64_t inner,
+                     int64_t num_groups, int dtype, void* stream);
+
+/*
+ * Bytes of workspace kat_rational_bwd needs for this problem on `device`
+ * (an upper bound over every pointer alignment).  No counterpart in the
+ * reference, whose backward allocates with torch.zeros inside the launcher
+ * (kat_rational/rational_triton.py:224-226).
+ */
+int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inner,
+                                    int64_t num_groups, int dtype, int device,
+                                    size_t* bytes);
+
+/* Human-readable text for a status code (static storage). */
+const char* kat_rational_strerror(int status);
+
+/* KAT_RATIONAL_ABI_VERSION of the loaded library. */
+int kat_rational_abi_version(void);
+
+/*
+ * Launch geometry chosen for a problem, for inspection and tests.  Pure host
+ * arithmetic: it touches no GPU.  `sm_count` and `ctas_per_sm` stand in for the
+ * device's multiprocessor count and the kernel's occupancy; `vec` is the
+ * elements-per-vector the kernels would use (0 = the widest the shape allows).
+ */
+typedef struct kat_rational_plan {
+  int64_t rows;          /* batch */
+  int64_t width;         /* channels * inner: elements per row */
+  int64_t group_width;   /* (channels / num_groups) * inner */
+  int64_t num_groups;
+  int32_t vec;           /* elements per vector load */
+  int32_t threads;       /* threads per block = tile_cols * tile_rows */
+  int32_t tile_cols;     /* vector columns per block */
+  int32_t tile_rows;     /* rows a block advances per step */
+  int64_t col_blocks;    /* blocks across a row */
+  int64_t items;         /* col_blocks * rows: the units split across blocks */
+  int64_t blocks;        /* grid size */
+  int32_t max_segments;  /* column blocks one block can touch */
+  int32_t max_local_groups;  /* groups one column block can touch */
+  uint64_t workspace_bytes;  /* backward partial-sum buffer */
+} kat_rational_plan;
+
+int kat_rational_make_plan(int64_t batch, int64_t channels, int64_t inner,
+                           int64_t num_groups, int dtype, int vec,
+                           int sm_count, int ctas_per_sm,
+                           kat_rational_plan* plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KAT_RATIONAL_H_ */

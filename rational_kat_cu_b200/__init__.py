@@ -1,0 +1,35 @@
+"""B200-native (sm_100a) group-rational activation for the Kolmogorov-Arnold Transformer.
+
+Public API, matching the reference package `kat_rational` (kat_rational/__init__.py:1-4):
+KAT_Group, KAT_Group2D, KAT_Group_Torch and the autograd Functions (also under their
+reference names RationalTriton1DGroup / RationalTriton2D).
+"""
+
+from .kat_1dgroup import KAT_Group
+from .kat_1dgroup_torch import KAT_Group_Torch, Rational_CUDA_A_1DGroup
+from .kat_2dgroup import KAT_Group2D
+from .rational_cuda import (
+    RationalCUDA1DGroup,
+    RationalCUDA2D,
+    RationalTriton1DGroup,
+    RationalTriton2D,
+    rational_bwd_cuda,
+    rational_bwd_cuda_2d,
+    rational_fwd_cuda,
+    rational_fwd_cuda_2d,
+)
+
+__all__ = [
+    "KAT_Group",
+    "KAT_Group2D",
+    "KAT_Group_Torch",
+    "Rational_CUDA_A_1DGroup",
+    "RationalCUDA1DGroup",
+    "RationalCUDA2D",
+    "RationalTriton1DGroup",
+    "RationalTriton2D",
+    "rational_fwd_cuda",
+    "rational_bwd_cuda",
+    "rational_fwd_cuda_2d",
+    "rational_bwd_cuda_2d",
+]

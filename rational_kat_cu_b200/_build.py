@@ -1,0 +1,63 @@
+"""Build recipe for libkat_rational.so (the sm_100a kernels behind the C ABI).
+
+`build()` runs nvcc on csrc/kat_rational.cu for `-gencode arch=compute_100a,code=sm_100a`
+and writes the shared library next to this file, so it travels with the source tree.
+It rebuilds only when the source or the public header is newer than the library.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+SOURCE = os.path.join(PKG_DIR, "csrc", "kat_rational.cu")
+HEADER = os.path.join(REPO_DIR, "include", "kat_rational.h")
+LIBRARY = os.path.join(PKG_DIR, "libkat_rational.so")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC,-O2",
+    "-shared",
+    "-diag-suppress", "177",
+]
+
+
+def find_nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
+
+
+def is_stale() -> bool:
+    if not os.path.exists(LIBRARY):
+        return True
+    lib_t = os.path.getmtime(LIBRARY)
+    return any(os.path.getmtime(p) > lib_t for p in (SOURCE, HEADER, __file__))
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile the library if needed; return its path."""
+    if not force and not is_stale():
+        return LIBRARY
+    cmd = [find_nvcc(), *NVCC_FLAGS, "-I", os.path.join(REPO_DIR, "include"),
+           "-o", LIBRARY + ".tmp", SOURCE]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    if verbose:
+        print(res.stderr, file=sys.stderr)
+    os.replace(LIBRARY + ".tmp", LIBRARY)
+    return LIBRARY
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,74 @@
+"""KAT_Group: group-rational activation for channels-last input ([B, L, C] or [B, C]).
+
+Drop-in for the reference's kat_rational/kat_1dgroup_triton.py:9-97: same constructor
+(num_groups=8, mode="gelu", device="cuda"), the same parameters
+(weight_numerator [1, 6] shared by all groups, weight_denominator [num_groups, 4], fp32,
+initialised from init.json) and the same forward, which repeats the numerator per group
+and calls the autograd Function.  With device="cuda" the Function is RationalCUDA1DGroup
+(sm_100a kernels); device="cpu" selects the explicit PyTorch CPU formulation, as the
+reference does (kat_1dgroup_triton.py:29-32).  The CUDA module never switches to the CPU
+formulation by itself: a CPU tensor given to it raises.
+"""
+
+from __future__ import annotations
+
+import json
+
+import torch
+import torch.nn as nn
+
+from ._init_table import INIT_JSON
+from .kat_1dgroup_torch import Rational_CUDA_A_1DGroup
+from .rational_cuda import RationalCUDA1DGroup
+
+
+class KAT_Group(nn.Module):
+    def __init__(self, num_groups: int = 8, mode: str = "gelu", device: str = "cuda"):
+        """
+        Args:
+            num_groups: number of channel groups, each with its own denominator.
+            mode: init.json preset for the coefficients ("gelu", "identity", ...).
+            device: "cuda" (sm_100a kernels) or "cpu" (PyTorch formulation).
+        """
+        super().__init__()
+        assert device in ["cuda", "cpu"], "Device must be either 'cuda' or 'cpu'."
+        self.order = (5, 4)
+        self.num_groups = num_groups
+        self.initialize(mode=mode)
+        if device == "cuda":
+            self.rational = RationalCUDA1DGroup.apply
+        else:
+            self.rational = Rational_CUDA_A_1DGroup
+
+    def init_info(self) -> dict:
+        """The init.json table."""
+        with open(INIT_JSON) as json_file:
+            return json.load(json_file)
+
+    def initialize(self, mode: str = "gelu") -> None:
+        """Set the coefficients from an init.json preset (kat_1dgroup_triton.py:46-70)."""
+        try:
+            with open(INIT_JSON) as json_file:
+                data = json.load(json_file)
+            weight_numerator = torch.tensor(data[mode]["init_w_numerator"]).view(1, -1)
+            weight_denominator = torch.tensor(data[mode]["init_w_denominator"])
+            weight_denominator = torch.cat([weight_denominator] * self.num_groups).view(
+                self.num_groups, -1)
+            self.weight_numerator = nn.Parameter(weight_numerator.float(), requires_grad=True)
+            self.weight_denominator = nn.Parameter(weight_denominator.float(), requires_grad=True)
+        except FileNotFoundError:
+            print("Initialization JSON file not found.")
+        except json.JSONDecodeError:
+            print("Error decoding JSON.")
+
+    def forward(self, input: torch.Tensor) -> torch.Tensor:
+        assert input.dim() == 3 or input.dim() == 2, \
+            "Input tensor must be 3D (batch, length, channels) or 2D (batch, channels)."
+        weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
+        if self.rational is Rational_CUDA_A_1DGroup and input.dim() == 2:
+            return self.rational(input.unsqueeze(0), weight_numerator, self.weight_denominator,
+                                 self.num_groups).squeeze(0)
+        return self.rational(input, weight_numerator, self.weight_denominator, self.num_groups)
+
+    def extra_repr(self) -> str:
+        return f"num_groups={self.num_groups}, order={self.order}"

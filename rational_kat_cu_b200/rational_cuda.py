@@ -1,0 +1,220 @@
+"""Host-side launchers and autograd Functions over the C ABI.
+
+Mirrors the reference's launcher/Function layer for the group-rational path:
+
+  rational_fwd_cuda / rational_bwd_cuda        <- kat_rational/rational_triton.py:76-94, 217-238
+  rational_fwd_cuda_2d / rational_bwd_cuda_2d  <- kat_rational/rational_triton2d.py:71-91, 194-220
+  RationalCUDA1DGroup (alias RationalTriton1DGroup) <- kat_rational/rational_triton.py:241-297
+  RationalCUDA2D (alias RationalTriton2D)      <- kat_rational/rational_triton2d.py:226-246
+
+Same argument meaning: `n` is the [group, 6] numerator (the module passes its
+[1, 6] parameter repeated per group), `d` the [group, 4] denominator; the
+backward returns (d_x, d_n[group, 6] fp32, d_d[group, 4] fp32).  The math is the
+reference's PyTorch formula (kat_rational/kat_1dgroup_torch.py:27-78), computed
+by the sm_100a kernels in libkat_rational.so; nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from . import _native
+
+_DTYPE_CODES = {
+    torch.float32: _native.KAT_DTYPE_F32,
+    torch.float16: _native.KAT_DTYPE_F16,
+    torch.bfloat16: _native.KAT_DTYPE_BF16,
+}
+
+_workspace_cache: dict = {}
+
+
+def _dtype_code(t: Tensor) -> int:
+    try:
+        return _DTYPE_CODES[t.dtype]
+    except KeyError:
+        raise TypeError(f"kat_rational: unsupported dtype {t.dtype} "
+                        f"(expected float32, float16 or bfloat16)") from None
+
+
+def _check_cuda(name: str, t: Tensor) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"kat_rational: {name} must be a CUDA tensor (got device {t.device}); "
+                           f"the CUDA path has no CPU implementation")
+
+
+def _check_counts(n: Tensor, d: Tensor, group: int) -> None:
+    assert n.numel() == group * 6, f"numerator: expected {group*6} coeffs, got {n.numel()}"
+    assert d.numel() == group * 4, f"denominator: expected {group*4} coeffs, got {d.numel()}"
+
+
+def _coefficients(n: Tensor, d: Tensor, group: int, device: torch.device):
+    _check_counts(n, d, group)
+    n32 = n.detach().to(device=device, dtype=torch.float32).contiguous()
+    d32 = d.detach().to(device=device, dtype=torch.float32).contiguous()
+    return n32, d32
+
+
+def _dims_1d(x: Tensor, group: int):
+    if x.dim() < 1:
+        raise ValueError("kat_rational: input must have a channel dimension")
+    channels = x.shape[-1]
+    if group < 1 or channels % group != 0:
+        raise ValueError(f"kat_rational: channels ({channels}) must be divisible by "
+                         f"num_groups ({group})")
+    batch = x.numel() // channels if channels else 0
+    return batch, channels, 1
+
+
+def _dims_2d(x: Tensor, group: int):
+    if x.dim() != 4:
+        raise ValueError(f"kat_rational: 2D input must be [B, C, H, W], got {tuple(x.shape)}")
+    b, c, h, w = x.shape
+    if group < 1 or c % group != 0:
+        raise ValueError(f"kat_rational: channels ({c}) must be divisible by num_groups ({group})")
+    return b, c, h * w
+
+
+def _stream_ptr(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _workspace_bytes(dims, group: int, code: int, device: torch.device) -> int:
+    key = (dims, group, code, device.index)
+    hit = _workspace_cache.get(key)
+    if hit is not None:
+        return hit
+    out = ctypes.c_size_t(0)
+    _native.check("kat_rational_bwd_workspace_size",
+                  _native.lib().kat_rational_bwd_workspace_size(
+                      dims[0], dims[1], dims[2], group, code, device.index, ctypes.byref(out)))
+    _workspace_cache[key] = out.value
+    return out.value
+
+
+def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims) -> Tensor:
+    _check_counts(n, d, group)
+    _check_cuda("input", x)
+    code = _dtype_code(x)
+    x = x.contiguous()
+    n32, d32 = _coefficients(n, d, group, x.device)
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    with torch.cuda.device(x.device):
+        status = _native.lib().kat_rational_fwd(
+            x.data_ptr(), y.data_ptr(), n32.data_ptr(), d32.data_ptr(),
+            dims[0], dims[1], dims[2], group, code, _stream_ptr(x.device))
+    _native.check("kat_rational_fwd", status)
+    return y
+
+
+def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
+         need_dx: bool = True):
+    _check_counts(n, d, group)
+    _check_cuda("input", x)
+    _check_cuda("grad_output", grad_output)
+    code = _dtype_code(x)
+    x = x.contiguous()
+    if grad_output.dtype != x.dtype:
+        grad_output = grad_output.to(x.dtype)
+    grad_output = grad_output.contiguous()
+    if grad_output.shape != x.shape:
+        raise ValueError(f"kat_rational: grad_output shape {tuple(grad_output.shape)} != "
+                         f"input shape {tuple(x.shape)}")
+    n32, d32 = _coefficients(n, d, group, x.device)
+    d_x = torch.empty_like(x, memory_format=torch.contiguous_format) if need_dx else None
+    d_n = torch.empty(n.shape, dtype=torch.float32, device=x.device)
+    d_d = torch.empty(d.shape, dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        ws_bytes = _workspace_bytes(dims, group, code, x.device)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
+        status = _native.lib().kat_rational_bwd(
+            x.data_ptr(), grad_output.data_ptr(), d_x.data_ptr() if d_x is not None else None,
+            n32.data_ptr(), d32.data_ptr(), d_n.data_ptr(), d_d.data_ptr(),
+            ws.data_ptr(), ws.numel(), dims[0], dims[1], dims[2], group, code,
+            _stream_ptr(x.device))
+    _native.check("kat_rational_bwd", status)
+    return d_x, d_n, d_d
+
+
+def rational_fwd_cuda(x: Tensor, n: Tensor, d: Tensor, group: int) -> Tensor:
+    """Forward for channels-last input ([..., C]); kat_rational/rational_triton.py:76-94."""
+    return _fwd(x, n, d, group, _dims_1d(x, group))
+
+
+def rational_bwd_cuda(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int):
+    """Backward for channels-last input; kat_rational/rational_triton.py:217-238.
+
+    Returns (d_x, d_n, d_d) with d_n/d_d fp32 and shaped like n/d.
+    """
+    return _bwd(grad_output, x, n, d, group, _dims_1d(x, group))
+
+
+def rational_fwd_cuda_2d(x: Tensor, n: Tensor, d: Tensor, group: int) -> Tensor:
+    """Forward for NCHW input; kat_rational/rational_triton2d.py:71-91."""
+    return _fwd(x, n, d, group, _dims_2d(x, group))
+
+
+def rational_bwd_cuda_2d(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int):
+    """Backward for NCHW input; kat_rational/rational_triton2d.py:194-220."""
+    return _bwd(grad_output, x, n, d, group, _dims_2d(x, group))
+
+
+class RationalCUDA1DGroup(torch.autograd.Function):
+    """Group-rational activation on channels-last input ([B, L, C] or [B, C]).
+
+    Drop-in for the reference's RationalTriton1DGroup (kat_rational/rational_triton.py:241-297):
+    same apply(input, weight_numerator[G,6], weight_denominator[G,4], group) signature, the
+    same custom_fwd(cast_inputs=float32) / custom_bwd autocast behaviour, and the backward
+    returns (d_input, d_numerator[G,6], d_denominator[G,4], None).
+    """
+
+    @staticmethod
+    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
+    def forward(ctx, input: Tensor, weight_numerator: Tensor, weight_denominator: Tensor,
+                group: int) -> Tensor:
+        ctx.save_for_backward(input, weight_numerator, weight_denominator)
+        ctx.group = group
+        return rational_fwd_cuda(input, weight_numerator, weight_denominator, group)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output: Tensor):
+        input, weight_numerator, weight_denominator = ctx.saved_tensors
+        group = ctx.group
+        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
+                                     group, _dims_1d(input, group),
+                                     need_dx=ctx.needs_input_grad[0])
+        return d_input, d_num, d_den, None
+
+
+class RationalCUDA2D(torch.autograd.Function):
+    """Group-rational activation on NCHW input ([B, C, H, W]).
+
+    Drop-in for the reference's RationalTriton2D (kat_rational/rational_triton2d.py:226-246).
+    """
+
+    @staticmethod
+    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
+    def forward(ctx, input: Tensor, weight_numerator: Tensor, weight_denominator: Tensor,
+                group: int) -> Tensor:
+        ctx.save_for_backward(input, weight_numerator, weight_denominator)
+        ctx.group = group
+        return rational_fwd_cuda_2d(input, weight_numerator, weight_denominator, group)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output: Tensor):
+        input, weight_numerator, weight_denominator = ctx.saved_tensors
+        group = ctx.group
+        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
+                                     group, _dims_2d(input, group),
+                                     need_dx=ctx.needs_input_grad[0])
+        return d_input, d_num, d_den, None
+
+
+# The reference's export names (kat_rational/__init__.py:2, rational_triton2d.py:226).
+RationalTriton1DGroup = RationalCUDA1DGroup
+RationalTriton2D = RationalCUDA2D
