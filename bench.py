@@ -351,6 +351,9 @@ def run_ours(args):
 
     fwd_ms = time_launches(lambda: fwd_fn(xs, n_rep, d_rep, w.groups), args.kernel_iters)
     bwd_ms = time_launches(lambda: bwd_fn(gy, xs, n_rep, d_rep, w.groups), args.kernel_iters)
+    mode = os.environ.get("KAT_RATIONAL_PIPELINE", "async")
+    bwd_kernel_name = {"registers": "kat_bwd_kernel", "bulk": "kat_bwd_tma_kernel"}.get(
+        mode, "kat_bwd_async_kernel") + " + kat_bwd_reduce_kernel (one C-ABI backward call)"
     fwd_gbs = 2 * N * elem_bytes / (fwd_ms * 1e-3) / 1e9
     bwd_gbs = 3 * N * elem_bytes / (bwd_ms * 1e-3) / 1e9
 
@@ -429,7 +432,7 @@ def run_ours(args):
                         + (" + NCCL coefficient-gradient all-gather" if world > 1 else ""),
             },
             "roofline": {
-                "bound": "hbm", "kernel": "kat_bwd_kernel (+ kat_bwd_reduce_kernel)",
+                "bound": "hbm", "kernel": bwd_kernel_name,
                 "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
                 "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
                 "algorithmic_bytes_per_launch": 3 * N * elem_bytes,

@@ -106,6 +106,15 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
                                     int64_t num_groups, int dtype, int device,
                                     size_t* bytes);
 
+/*
+ * Sticky device-side status word of `device`: 0, or KAT_DEVICE_WAIT_TIMEOUT when a
+ * pipelined kernel gave up on a bounded wait (its outputs are then undefined).  Reads the
+ * word synchronously (waits for the device's pending work); reset != 0 clears it.
+ * No counterpart in the reference, whose kernels have no device-side waits.
+ */
+#define KAT_DEVICE_WAIT_TIMEOUT 1
+int kat_rational_device_status(int device, int reset, int* status);
+
 /* Human-readable text for a status code (static storage). */
 const char* kat_rational_strerror(int status);
 

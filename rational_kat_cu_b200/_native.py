@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "kat_rational_strerror",
     "kat_rational_abi_version",
     "kat_rational_make_plan",
+    "kat_rational_device_status",
 )
 
 ABI_VERSION = 1
@@ -74,7 +75,8 @@ _lib = None
 
 
 def library_path() -> str:
-    return _build.LIBRARY
+    """The in-tree library, or KAT_RATIONAL_LIBRARY when set (an alternative build)."""
+    return os.environ.get("KAT_RATIONAL_LIBRARY") or _build.LIBRARY
 
 
 def _declare(lib: ctypes.CDLL) -> None:
@@ -94,6 +96,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_make_plan.argtypes = [i64, i64, i64, i64, i32, i32, i32, i32,
                                            ctypes.POINTER(KatPlan)]
     lib.kat_rational_make_plan.restype = i32
+    lib.kat_rational_device_status.argtypes = [i32, i32, ctypes.POINTER(ctypes.c_int)]
+    lib.kat_rational_device_status.restype = i32
 
 
 def lib() -> ctypes.CDLL:
@@ -124,6 +128,14 @@ def strerror(status: int) -> str:
 def check(func: str, status: int) -> None:
     if status != KAT_OK:
         raise KatError(func, status, strerror(status))
+
+
+def device_status(device: int = 0, reset: bool = False) -> int:
+    """Sticky device status word (0 = no kernel gave up on a bounded wait)."""
+    out = ctypes.c_int(0)
+    check("kat_rational_device_status",
+          lib().kat_rational_device_status(device, 1 if reset else 0, ctypes.byref(out)))
+    return out.value
 
 
 def make_plan(batch: int, channels: int, inner: int, num_groups: int, dtype: int,

@@ -37,8 +37,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <type_traits>
 #include <mutex>
@@ -118,8 +120,10 @@ template <> struct Codec<float> {
 
 template <> struct Codec<__nv_bfloat16> {
   static constexpr int kBytes = 2;
+  // Byte permutes run on the integer ALU, keeping the FMA pipe for the arithmetic.
   __device__ __forceinline__ static float2 unpack_word(uint32_t w) {
-    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    return make_float2(__uint_as_float(__byte_perm(w, 0u, 0x1044u)),
+                       __uint_as_float(__byte_perm(w, 0u, 0x3244u)));
   }
   __device__ __forceinline__ static uint32_t pack_word(float2 f) {
     __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
@@ -169,10 +173,17 @@ template <typename Tio, int V> struct RawOf {
 };
 template <> struct RawOf<float, 1> { using T = uint32_t; };
 
+// Read-only streaming load; 16-byte vectors skip L1 and ask L2 for 256-byte fetches.
 template <typename Tio, int V>
 __device__ __forceinline__ typename RawOf<Tio, V>::T load_raw(const Tio* __restrict__ ptr) {
   using B = typename RawOf<Tio, V>::T;
-  if constexpr (sizeof(B) == 2) {
+  if constexpr (sizeof(B) == 16) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(ptr));
+    return v;
+  } else if constexpr (sizeof(B) == 2) {
     return __ldg(reinterpret_cast<const unsigned short*>(ptr));
   } else {
     return __ldg(reinterpret_cast<const B*>(ptr));
@@ -276,8 +287,6 @@ template <typename L> struct FwdCoef {
 template <typename L> struct BwdCoef {
   L a0, a1, a2, a3, a4, a5;  // numerator
   L c1, c2, c3, c4;          // |b_i|
-  L p1, p2, p3, p4, p5;      // k * a_k: coefficients of P'
-  L q2, q3, q4;              // i * |b_i| for i = 2..4 (q1 = c1): coefficients of Q'
   L one;
 };
 
@@ -300,16 +309,10 @@ __device__ __forceinline__ void load_bwd_coef(const float* __restrict__ num,
                                               BwdCoef<L>& c) {
   const float* a = num + g * 6;
   const float* b = den + g * 4;
-  const float a0 = __ldg(a + 0), a1 = __ldg(a + 1), a2 = __ldg(a + 2);
-  const float a3 = __ldg(a + 3), a4 = __ldg(a + 4), a5 = __ldg(a + 5);
-  const float c1 = fabsf(__ldg(b + 0)), c2 = fabsf(__ldg(b + 1));
-  const float c3 = fabsf(__ldg(b + 2)), c4 = fabsf(__ldg(b + 3));
-  c.a0 = bcast<L>(a0); c.a1 = bcast<L>(a1); c.a2 = bcast<L>(a2);
-  c.a3 = bcast<L>(a3); c.a4 = bcast<L>(a4); c.a5 = bcast<L>(a5);
-  c.c1 = bcast<L>(c1); c.c2 = bcast<L>(c2); c.c3 = bcast<L>(c3); c.c4 = bcast<L>(c4);
-  c.p1 = bcast<L>(a1); c.p2 = bcast<L>(2.0f * a2); c.p3 = bcast<L>(3.0f * a3);
-  c.p4 = bcast<L>(4.0f * a4); c.p5 = bcast<L>(5.0f * a5);
-  c.q2 = bcast<L>(2.0f * c2); c.q3 = bcast<L>(3.0f * c3); c.q4 = bcast<L>(4.0f * c4);
+  c.a0 = bcast<L>(__ldg(a + 0)); c.a1 = bcast<L>(__ldg(a + 1)); c.a2 = bcast<L>(__ldg(a + 2));
+  c.a3 = bcast<L>(__ldg(a + 3)); c.a4 = bcast<L>(__ldg(a + 4)); c.a5 = bcast<L>(__ldg(a + 5));
+  c.c1 = bcast<L>(fabsf(__ldg(b + 0))); c.c2 = bcast<L>(fabsf(__ldg(b + 1)));
+  c.c3 = bcast<L>(fabsf(__ldg(b + 2))); c.c4 = bcast<L>(fabsf(__ldg(b + 3)));
   c.one = bcast<L>(1.0f);
 }
 
@@ -336,31 +339,33 @@ __device__ __forceinline__ L fwd_math(L x, const FwdCoef<L>& c) {
 // acc[0..5] (sum u x^k) and acc[6..9] (sum u y x^i, i = 1..4).
 template <typename L, bool kRefine>
 __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[kAcc]) {
+  // Horner for P and Q; the derivatives come from the same partial sums
+  // (d_k = d_{k+1} x + p_{k+1}), so no scaled coefficients are needed.
   L p = fma_(c.a5, x, c.a4);
+  L dp = fma_(c.a5, x, p);
   p = fma_(p, x, c.a3);
+  dp = fma_(dp, x, p);
   p = fma_(p, x, c.a2);
+  dp = fma_(dp, x, p);
   p = fma_(p, x, c.a1);
+  dp = fma_(dp, x, p);
   p = fma_(p, x, c.a0);
   L q = fma_(c.c4, x, c.c3);
+  L dq = fma_(c.c4, x, q);
   q = fma_(q, x, c.c2);
+  dq = fma_(dq, x, q);
   q = fma_(q, x, c.c1);
+  dq = fma_(dq, x, q);
   q = fma_(q, x, c.one);
-  L dp = fma_(c.p5, x, c.p4);
-  dp = fma_(dp, x, c.p3);
-  dp = fma_(dp, x, c.p2);
-  dp = fma_(dp, x, c.p1);
-  L dq = fma_(c.q4, x, c.q3);
-  dq = fma_(dq, x, c.q2);
-  dq = fma_(dq, x, c.c1);
   L r = rcp_(q);
   if constexpr (kRefine) {  // Newton-Raphson: r <- r + r (1 - q r)
     const L e = fma_(neg_(q), r, c.one);
     r = fma_(r, e, r);
   }
-  const L u = mul_(go, r);         // go / Q
-  const L y = mul_(p, r);          // P / Q
+  const L u = mul_(go, r);            // go / Q
+  const L y = mul_(p, r);             // P / Q
   const L t = fma_(neg_(y), dq, dp);  // P' - y Q'
-  const L w = mul_(u, y);          // go P / Q^2
+  const L w = mul_(u, y);             // go P / Q^2
   const L x2 = mul_(x, x);
   const L x3 = mul_(x2, x);
   const L x4 = mul_(x2, x2);
@@ -414,10 +419,65 @@ __device__ __forceinline__ void block_items(const Plan& p, int64_t blk, int64_t&
   i1 = p.items * (blk + 1) / p.blocks;
 }
 
+// Per-block, per-group reduction of one segment's per-thread sums (fixed order):
+// thread t of the `nthreads` participants stores its 10 sums, then warp w reduces
+// outputs w, w + nwarps, ... (output = local group x coefficient slot) in fp64 with a
+// fixed lane assignment and xor tree, and writes them to the block's workspace slots.
+// kNamed selects a named barrier over the participants (warp-specialised kernels)
+// instead of __syncthreads.
+template <bool kNamed>
+__device__ __forceinline__ void participants_sync(int nthreads) {
+  if constexpr (kNamed) {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+  } else {
+    __syncthreads();
+  }
+}
+
+template <bool kNamed>
+__device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float* s_acc,
+                                               int stride, int tid, int nthreads, const Plan& p,
+                                               int64_t cb, int64_t seg, int64_t blk,
+                                               double* __restrict__ partial) {
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k) s_acc[k * stride + tid] = sums[k];
+  participants_sync<kNamed>(nthreads);
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nwarps = nthreads >> 5;
+  const int64_t col0 = cb * p.tile_cols;
+  const int64_t col_end = min(col0 + p.tile_cols, p.vec_cols);
+  const int64_t g_first = col0 / p.vec_group;
+  const int64_t g_last = (col_end - 1) / p.vec_group;
+  const int n_out = int(g_last - g_first + 1) * kAcc;
+  for (int o = warp; o < n_out; o += nwarps) {
+    const int lg = o / kAcc;
+    const int k = o - lg * kAcc;
+    const int64_t g = g_first + lg;
+    const int tlo = int(max(g * p.vec_group, col0) - col0);
+    const int thi = int(min((g + 1) * p.vec_group, col_end) - col0);
+    const int wcols = thi - tlo;
+    const int n = wcols * p.tile_rows;
+    double v = 0.0;
+    for (int j = lane; j < n; j += 32) {
+      const int jr = j / wcols;
+      const int jc = tlo + (j - jr * wcols);
+      v += double(s_acc[k * stride + jr * p.tile_cols + jc]);
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    if (lane == 0) partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+  }
+  participants_sync<kNamed>(nthreads);
+}
+
 // ---------------------------------------------------------------------------
 // Forward kernel.
 // ---------------------------------------------------------------------------
 
+// Rows handled by thread row `tr` inside a segment start at r0 and step by tile_rows;
+// they are processed U at a time, and the next U rows are loaded before the current
+// ones are computed, so every thread keeps loads in flight while it computes.
 template <typename Tio, int V, int U>
 __global__ void __launch_bounds__(kMaxThreads)
 kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
@@ -430,36 +490,37 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
   if (tr >= p.tile_rows) return;
   int64_t i0, i1;
   block_items(p, blockIdx.x, i0, i1);
-  const int64_t row_step = int64_t(p.tile_rows) * p.width;
+  const int64_t step = int64_t(p.tile_rows) * p.width;
   for (int64_t i = i0; i < i1;) {
     const int64_t cb = i / p.rows;
     const int64_t seg_end = min(i1, (cb + 1) * p.rows);
     const int64_t col = cb * p.tile_cols + tc;
-    if (col < p.vec_cols) {
+    const int64_t r0 = i - cb * p.rows + tr;
+    const int64_t r_end = seg_end - cb * p.rows;
+    if (col < p.vec_cols && r0 < r_end) {
       FwdCoef<L> c;
       load_fwd_coef<L>(num, den, col / p.vec_group, c);
-      const int64_t r1 = seg_end - cb * p.rows;
-      int64_t r = i - cb * p.rows + tr;
-      const int64_t off = r * p.width + col * V;
-      const Tio* xp = x + off;
-      Tio* yp = y + off;
-#pragma unroll 1
-      for (; r + (U - 1) * p.tile_rows < r1; r += U * p.tile_rows) {
-        Raw raw[U];
+      const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
+      const Tio* xp = x + r0 * p.width + col * V;
+      Tio* yp = y + r0 * p.width + col * V;
+      Raw cur[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) raw[u] = load_raw<Tio, V>(xp + u * row_step);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          store_raw<Tio, V>(yp + u * row_step, fwd_vec<Tio, V, L, kExact>(raw[u], c));
-        }
-        xp += U * row_step;
-        yp += U * row_step;
-      }
+      for (int u = 0; u < U; ++u)
+        if (u < n) cur[u] = load_raw<Tio, V>(xp + u * step);
+      xp += U * step;
 #pragma unroll 1
-      for (; r < r1; r += p.tile_rows) {
-        store_raw<Tio, V>(yp, fwd_vec<Tio, V, L, kExact>(load_raw<Tio, V>(xp), c));
-        xp += row_step;
-        yp += row_step;
+      for (int64_t b = 0; b < n; b += U) {
+        Raw nxt[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (b + U + u < n) nxt[u] = load_raw<Tio, V>(xp + u * step);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (b + u < n) store_raw<Tio, V>(yp + u * step, fwd_vec<Tio, V, L, kExact>(cur[u], c));
+#pragma unroll
+        for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+        xp += U * step;
+        yp += U * step;
       }
     }
     i = seg_end;
@@ -484,13 +545,10 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
   const int tr = threadIdx.x / p.tile_cols;
   const bool row_thread = tr < p.tile_rows;
   const bool write_dx = dx != nullptr;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
 
   int64_t i0, i1;
   block_items(p, blockIdx.x, i0, i1);
-  const int64_t row_step = int64_t(p.tile_rows) * p.width;
+  const int64_t step = int64_t(p.tile_rows) * p.width;
   const int64_t cb0 = i0 / p.rows;
 
   for (int64_t i = i0; i < i1;) {
@@ -501,73 +559,176 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) acc[k] = bcast<L>(0.0f);
 
-    if (row_thread && col < p.vec_cols) {
+    const int64_t r0 = i - cb * p.rows + tr;
+    const int64_t r_end = seg_end - cb * p.rows;
+    if (row_thread && col < p.vec_cols && r0 < r_end) {
       BwdCoef<L> c;
       load_bwd_coef<L>(num, den, col / p.vec_group, c);
-      const int64_t r1 = seg_end - cb * p.rows;
-      int64_t r = i - cb * p.rows + tr;
-      const int64_t off = r * p.width + col * V;
+      const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
+      const int64_t off = r0 * p.width + col * V;
       const Tio* xp = x + off;
       const Tio* gp = gy + off;
       Tio* dp = write_dx ? dx + off : nullptr;
-#pragma unroll 1
-      for (; r + (U - 1) * p.tile_rows < r1; r += U * p.tile_rows) {
-        Raw rx[U], rg[U];
+      Raw cx[U], cg[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          rx[u] = load_raw<Tio, V>(xp + u * row_step);
-          rg[u] = load_raw<Tio, V>(gp + u * row_step);
+      for (int u = 0; u < U; ++u) {
+        if (u < n) {
+          cx[u] = load_raw<Tio, V>(xp + u * step);
+          cg[u] = load_raw<Tio, V>(gp + u * step);
         }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const Raw d = bwd_vec<Tio, V, L, kRefine>(rx[u], rg[u], c, acc);
-          if (write_dx) store_raw<Tio, V>(dp + u * row_step, d);
-        }
-        xp += U * row_step;
-        gp += U * row_step;
-        if (write_dx) dp += U * row_step;
       }
+      xp += U * step;
+      gp += U * step;
 #pragma unroll 1
-      for (; r < r1; r += p.tile_rows) {
-        const Raw d = bwd_vec<Tio, V, L, kRefine>(load_raw<Tio, V>(xp), load_raw<Tio, V>(gp), c, acc);
-        if (write_dx) store_raw<Tio, V>(dp, d);
-        xp += row_step;
-        gp += row_step;
-        if (write_dx) dp += row_step;
+      for (int64_t b = 0; b < n; b += U) {
+        Raw nx[U], ng[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (b + U + u < n) {
+            nx[u] = load_raw<Tio, V>(xp + u * step);
+            ng[u] = load_raw<Tio, V>(gp + u * step);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (b + u < n) {
+            const Raw d = bwd_vec<Tio, V, L, kRefine>(cx[u], cg[u], c, acc);
+            if (write_dx) store_raw<Tio, V>(dp + u * step, d);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          cx[u] = nx[u];
+          cg[u] = ng[u];
+        }
+        xp += U * step;
+        gp += U * step;
+        if (write_dx) dp += U * step;
       }
     }
 
     // Block reduction of this segment, per group, in a fixed order.
+    float sums[kAcc];
 #pragma unroll
-    for (int k = 0; k < kAcc; ++k) s_acc[k][threadIdx.x] = lane_sum(acc[k]);
-    __syncthreads();
-    const int64_t col0 = cb * p.tile_cols;
-    const int64_t col_end = min(col0 + p.tile_cols, p.vec_cols);
-    const int64_t g_first = col0 / p.vec_group;
-    const int64_t g_last = (col_end - 1) / p.vec_group;
-    const int n_out = int(g_last - g_first + 1) * kAcc;
-    const int64_t seg = cb - cb0;
-    for (int o = warp; o < n_out; o += nwarps) {
-      const int lg = o / kAcc;
-      const int k = o - lg * kAcc;
-      const int64_t g = g_first + lg;
-      const int tlo = int(max(g * p.vec_group, col0) - col0);
-      const int thi = int(min((g + 1) * p.vec_group, col_end) - col0);
-      const int wcols = thi - tlo;
-      const int n = wcols * p.tile_rows;
-      double s = 0.0;
-      for (int j = lane; j < n; j += 32) {
-        const int jr = j / wcols;
-        const int jc = tlo + (j - jr * wcols);
-        s += double(s_acc[k][jr * p.tile_cols + jc]);
-      }
+    for (int k = 0; k < kAcc; ++k) sums[k] = lane_sum(acc[k]);
+    segment_reduce<false>(sums, &s_acc[0][0], kMaxThreads, threadIdx.x, blockDim.x, p, cb,
+                          cb - cb0, blockIdx.x, partial);
+    i = seg_end;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward with a per-thread cp.async ring (16-byte vectors).
+//
+// Each thread streams its own future vectors of x and grad_out into a private ring of
+// kStages slots (kRows rows each) in shared memory with cp.async (16-byte, L1-bypassing,
+// 256-byte L2 fetch), one commit group per batch, and reads a batch back once
+// cp.async.wait_group shows it landed.  Loads in flight live in shared memory instead of
+// registers, so two blocks fit per SM and each keeps (kStages - 1) batches in flight.
+// Slot layout: [stage][row][tensor][thread] of 16-byte vectors (conflict-free).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename Tio, int kStages, int kRows>
+__global__ void __launch_bounds__(kMaxThreads)
+kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
+                     const float* __restrict__ num, const float* __restrict__ den,
+                     double* __restrict__ partial, const Plan p) {
+  constexpr int V = 16 / sizeof(Tio);
+  constexpr bool kRefine = sizeof(Tio) == 4;
+  extern __shared__ __align__(16) uint4 ring[];
+  const int T = blockDim.x;
+  float* s_acc = reinterpret_cast<float*>(ring + size_t(kStages) * kRows * 2 * T);
+  const int tid = threadIdx.x;
+  const int tc = tid % p.tile_cols;
+  const int tr = tid / p.tile_cols;
+  const bool row_thread = tr < p.tile_rows;
+  const bool write_dx = dx != nullptr;
+  int64_t i0, i1;
+  block_items(p, blockIdx.x, i0, i1);
+  const int64_t step = int64_t(p.tile_rows) * p.width;
+  const int64_t cb0 = i0 / p.rows;
+  uint4* const ring_t = ring + tid;
+  const int slot_stride = 2 * T;            // uint4s between rows of a stage
+  const int stage_stride = kRows * 2 * T;   // uint4s between stages
+
+  for (int64_t i = i0; i < i1;) {
+    const int64_t cb = i / p.rows;
+    const int64_t seg_end = min(i1, (cb + 1) * p.rows);
+    const int64_t col = cb * p.tile_cols + tc;
+    const int64_t r0 = i - cb * p.rows + tr;
+    const int64_t r_end = seg_end - cb * p.rows;
+    float2 acc[kAcc];
 #pragma unroll
-      for (int m = 16; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-      if (lane == 0) {
-        partial[((int64_t(blockIdx.x) * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = s;
+    for (int k = 0; k < kAcc; ++k) acc[k] = make_float2(0.0f, 0.0f);
+    if (row_thread && col < p.vec_cols && r0 < r_end) {
+      BwdCoef<float2> c;
+      load_bwd_coef<float2>(num, den, col / p.vec_group, c);
+      const int n = int(min(int64_t(0x7fffffff), (r_end - r0 + p.tile_rows - 1) / p.tile_rows));
+      const int nb = (n + kRows - 1) / kRows;
+      const int64_t off = r0 * p.width + col * V;
+      const Tio* lx = x + off;   // next rows to load
+      const Tio* lg = gy + off;
+      Tio* dp = write_dx ? dx + off : nullptr;
+      int load_stage = 0;
+      int load_row = 0;
+      // Issue the loads of the next batch (rows load_row .. load_row + kRows - 1).
+      auto issue = [&]() {
+        uint4* sp = ring_t + load_stage * stage_stride;
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          if (load_row + u < n) {
+            cp_async16(sp + u * slot_stride, lx);
+            cp_async16(sp + u * slot_stride + T, lg);
+            lx += step;
+            lg += step;
+          }
+        }
+        load_row += kRows;
+        load_stage = load_stage + 1 == kStages ? 0 : load_stage + 1;
+        cp_async_commit();
+      };
+#pragma unroll
+      for (int b = 0; b < kStages - 1; ++b) issue();
+      int use_stage = 0;
+#pragma unroll 1
+      for (int b = 0; b < nb; ++b) {
+        issue();
+        cp_async_wait<kStages - 1>();
+        const uint4* sp = ring_t + use_stage * stage_stride;
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          if (b * kRows + u < n) {
+            const uint4 rx = sp[u * slot_stride];
+            const uint4 rg = sp[u * slot_stride + T];
+            const uint4 d = bwd_vec<Tio, V, float2, kRefine>(rx, rg, c, acc);
+            if (write_dx) {
+              store_raw<Tio, V>(dp, d);
+              dp += step;
+            }
+          }
+        }
+        use_stage = use_stage + 1 == kStages ? 0 : use_stage + 1;
       }
+      cp_async_wait<0>();
     }
-    __syncthreads();
+    float sums[kAcc];
+#pragma unroll
+    for (int k = 0; k < kAcc; ++k) sums[k] = lane_sum(acc[k]);
+    segment_reduce<false>(sums, s_acc, T, tid, T, p, cb, cb - cb0, blockIdx.x, partial);
     i = seg_end;
   }
 }
@@ -612,10 +773,329 @@ kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restric
 }
 
 // ---------------------------------------------------------------------------
+// Bulk-copy pipelined kernels (16-byte vectors).
+//
+// Warp 0 is the producer: one lane streams the block's tiles (stage_rows rows of its
+// column block, for x and — backward — grad_out) from global memory into a ring of
+// `stages` shared-memory slots with cp.async.bulk, each slot guarded by a "full"
+// mbarrier (transaction-counted) and an "empty" mbarrier (one arrival per consumer
+// warp).  The other warps consume: each thread keeps its fixed vector column, reads its
+// vectors from shared memory, computes, and stores y / dx straight to global memory.
+// The ring keeps up to stages x stage bytes of loads in flight per SM without holding
+// them in registers.  Every wait is bounded (about two seconds of clock cycles); a wait
+// that runs out sets the block's abort flag and the sticky device status word, and the
+// block then runs to completion without further waiting.
+// ---------------------------------------------------------------------------
+
+struct Pipe {
+  int32_t stages;       // ring depth
+  int32_t stage_rows;   // rows per slot (multiple of tile_rows)
+  int32_t seg_bytes;    // bytes of one row slot = tile_cols * 16
+  int32_t contiguous;   // 1: a slot is one contiguous global range per tensor
+  uint32_t smem_bytes;  // dynamic shared memory per block
+  uint32_t chunk_bytes; // largest single bulk copy (multiple of 16)
+  int32_t poll_ns;      // < 0: every lane polls; >= 0: lane 0 polls with this back-off
+};
+
+constexpr int kStatusWaitTimeout = 1;
+constexpr long long kWaitCycles = 4000000000LL;
+constexpr uint32_t kPipeHeader = 256;  // barriers + abort flag, keeps slots 128-byte aligned
+
+__device__ int g_kat_status;  // sticky device status (0 = ok), read by kat_rational_device_status
+
+__device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Slot release by a consumer warp.  Relaxed: the slot only guards this warp's shared-memory
+// reads (complete once their values were used); a release arrive would also wait for the
+// warp's preceding global stores to be performed.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+// Non-suspending test of the phase with `parity` (mbarrier.test_wait): the waits below
+// poll it, so a released slot is seen at once (try_wait may park the thread for a
+// system-dependent time first).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bulk global -> shared copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// completing as transactions on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Consumer-warp wait: lane 0 polls with a short back-off, then every lane observes the
+// completed phase itself (acquire), so the bulk-copied data is visible to all lanes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int backoff_ns) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0) {
+    const long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+      if (*abort) { ok = false; break; }
+      if (clock64() - t0 > kWaitCycles) {
+        *abort = 1;
+        atomicExch(&g_kat_status, kStatusWaitTimeout);
+        ok = false;
+        break;
+      }
+      if (backoff_ns > 0) __nanosleep(backoff_ns);
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (ok) mbar_wait(bar, parity, abort);
+  return ok;
+}
+
+// Bounded wait for the phase with `parity` of `bar`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_test(bar, parity)) return true;
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      atomicExch(&g_kat_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// The block's tiles, in order: consecutive runs of up to stage_rows rows that stay in
+// one column block.
+struct TileCursor {
+  int64_t i, i1;
+  __device__ TileCursor(const Plan& p, int64_t blk) { block_items(p, blk, i, i1); }
+  __device__ bool next(const Plan& p, int stage_rows, int64_t& cb, int64_t& row, int& nrows,
+                       bool& seg_last) {
+    if (i >= i1) return false;
+    cb = i / p.rows;
+    row = i - cb * p.rows;
+    const int64_t seg_end = min(i1, (cb + 1) * p.rows);
+    const int64_t n = min(int64_t(stage_rows), seg_end - i);
+    nrows = int(n);
+    i += n;
+    seg_last = i == seg_end;
+    return true;
+  }
+};
+
+// Producer lane: stream the block's tiles of `kTensors` inputs into the ring.
+template <typename Tio, int kTensors>
+__device__ __forceinline__ void produce(const Tio* __restrict__ in0, const Tio* __restrict__ in1,
+                                        const Plan& p, const Pipe& q, uint64_t* full,
+                                        uint64_t* empty, char* slots, volatile int* abort) {
+  constexpr int V = 16 / sizeof(Tio);
+  TileCursor cur(p, blockIdx.x);
+  int64_t cb, row;
+  int nrows;
+  bool last;
+  const uint32_t slot_bytes = uint32_t(q.stage_rows) * uint32_t(q.seg_bytes);
+  for (uint32_t k = 0; cur.next(p, q.stage_rows, cb, row, nrows, last); ++k) {
+    const uint32_t s = k % uint32_t(q.stages);
+    if (k >= uint32_t(q.stages) && !mbar_wait(&empty[s], ((k / q.stages) - 1) & 1u, abort)) break;
+    const int64_t col0 = cb * p.tile_cols;
+    const uint32_t row_bytes = uint32_t(min(int64_t(p.tile_cols), p.vec_cols - col0)) * 16u;
+    mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(nrows) * kTensors);
+#pragma unroll
+    for (int t = 0; t < kTensors; ++t) {
+      const Tio* base = (t == 0 ? in0 : in1) + row * p.width + col0 * V;
+      char* dst = slots + (size_t(s) * kTensors + t) * slot_bytes;
+      if (q.contiguous) {
+        const char* src = reinterpret_cast<const char*>(base);
+        const uint32_t total = row_bytes * uint32_t(nrows);
+        for (uint32_t off = 0; off < total; off += q.chunk_bytes)
+          bulk_load(dst + off, src + off, min(q.chunk_bytes, total - off), &full[s]);
+      } else {
+        for (int j = 0; j < nrows; ++j) {
+          const char* src = reinterpret_cast<const char*>(base + int64_t(j) * p.width);
+          char* d = dst + size_t(j) * q.seg_bytes;
+          for (uint32_t off = 0; off < row_bytes; off += q.chunk_bytes)
+            bulk_load(d + off, src + off, min(q.chunk_bytes, row_bytes - off), &full[s]);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void pipe_init(uint64_t* full, uint64_t* empty, volatile int* abort,
+                                          int stages, int consumer_warps) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], uint32_t(consumer_warps));
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+}
+
+template <typename Tio>
+__global__ void __launch_bounds__(kMaxThreads + 32)
+kat_fwd_tma_kernel(const Tio* __restrict__ x, Tio* __restrict__ y, const float* __restrict__ num,
+                   const float* __restrict__ den, const Plan p, const Pipe q) {
+  constexpr int V = 16 / sizeof(Tio);
+  using Raw = uint4;
+  constexpr bool kExact = sizeof(Tio) == 4;
+  extern __shared__ __align__(128) char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + q.stages;
+  volatile int* abort = reinterpret_cast<volatile int*>(empty + q.stages);
+  char* slots = smem + kPipeHeader;
+  const int consumer_warps = int(blockDim.x >> 5) - 1;
+  pipe_init(full, empty, abort, q.stages, consumer_warps);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0) produce<Tio, 1>(x, nullptr, p, q, full, empty, slots, abort);
+    return;
+  }
+  const int ctid = threadIdx.x - 32;
+  const int tc = ctid % p.tile_cols;
+  const int tr = ctid / p.tile_cols;
+  const bool row_thread = tr < p.tile_rows;
+  const uint32_t slot_bytes = uint32_t(q.stage_rows) * uint32_t(q.seg_bytes);
+  TileCursor cur(p, blockIdx.x);
+  int64_t cb, row, cb_coef = -1;
+  int nrows;
+  bool last;
+  FwdCoef<float2> c;
+  for (uint32_t k = 0; cur.next(p, q.stage_rows, cb, row, nrows, last); ++k) {
+    const uint32_t s = k % uint32_t(q.stages);
+    if (q.poll_ns < 0) mbar_wait(&full[s], (k / q.stages) & 1u, abort);
+    else warp_wait(&full[s], (k / q.stages) & 1u, abort, q.poll_ns);
+    const int64_t col = cb * p.tile_cols + tc;
+    if (row_thread && col < p.vec_cols) {
+      if (cb != cb_coef) {
+        load_fwd_coef<float2>(num, den, col / p.vec_group, c);
+        cb_coef = cb;
+      }
+      const char* src = slots + size_t(s) * slot_bytes + size_t(tc) * 16;
+      Tio* dst = y + row * p.width + col * V;
+      for (int j = tr; j < nrows; j += p.tile_rows) {
+        const Raw raw = *reinterpret_cast<const Raw*>(src + size_t(j) * q.seg_bytes);
+        store_raw<Tio, V>(dst + int64_t(j) * p.width, fwd_vec<Tio, V, float2, kExact>(raw, c));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_relaxed(&empty[s]);
+  }
+}
+
+template <typename Tio>
+__global__ void __launch_bounds__(kMaxThreads + 32)
+kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
+                   const float* __restrict__ num, const float* __restrict__ den,
+                   double* __restrict__ partial, const Plan p, const Pipe q) {
+  constexpr int V = 16 / sizeof(Tio);
+  using Raw = uint4;
+  constexpr bool kRefine = sizeof(Tio) == 4;
+  extern __shared__ __align__(128) char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + q.stages;
+  volatile int* abort = reinterpret_cast<volatile int*>(empty + q.stages);
+  char* slots = smem + kPipeHeader;
+  const uint32_t slot_bytes = uint32_t(q.stage_rows) * uint32_t(q.seg_bytes);
+  float* s_acc = reinterpret_cast<float*>(slots + size_t(q.stages) * 2 * slot_bytes);
+  const int consumer_warps = int(blockDim.x >> 5) - 1;
+  pipe_init(full, empty, abort, q.stages, consumer_warps);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp == 0) {
+    if (lane == 0) produce<Tio, 2>(x, gy, p, q, full, empty, slots, abort);
+    return;
+  }
+  const int nthreads = consumer_warps * 32;
+  const int ctid = threadIdx.x - 32;
+  const int tc = ctid % p.tile_cols;
+  const int tr = ctid / p.tile_cols;
+  const bool row_thread = tr < p.tile_rows;
+  const bool write_dx = dx != nullptr;
+  int64_t i0, i1;
+  block_items(p, blockIdx.x, i0, i1);
+  const int64_t cb0 = i0 / p.rows;
+  TileCursor cur(p, blockIdx.x);
+  int64_t cb, row, cb_coef = -1;
+  int nrows;
+  bool last;
+  BwdCoef<float2> c;
+  float2 acc[kAcc];
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k) acc[k] = make_float2(0.0f, 0.0f);
+  for (uint32_t k = 0; cur.next(p, q.stage_rows, cb, row, nrows, last); ++k) {
+    const uint32_t s = k % uint32_t(q.stages);
+    if (q.poll_ns < 0) mbar_wait(&full[s], (k / q.stages) & 1u, abort);
+    else warp_wait(&full[s], (k / q.stages) & 1u, abort, q.poll_ns);
+    const int64_t col = cb * p.tile_cols + tc;
+    if (row_thread && col < p.vec_cols) {
+      if (cb != cb_coef) {
+        load_bwd_coef<float2>(num, den, col / p.vec_group, c);
+        cb_coef = cb;
+      }
+      const char* xs = slots + (size_t(s) * 2) * slot_bytes + size_t(tc) * 16;
+      const char* gs = xs + slot_bytes;
+      Tio* dst = write_dx ? dx + row * p.width + col * V : nullptr;
+      for (int j = tr; j < nrows; j += p.tile_rows) {
+        const Raw rx = *reinterpret_cast<const Raw*>(xs + size_t(j) * q.seg_bytes);
+        const Raw rg = *reinterpret_cast<const Raw*>(gs + size_t(j) * q.seg_bytes);
+        const Raw d = bwd_vec<Tio, V, float2, kRefine>(rx, rg, c, acc);
+        if (write_dx) store_raw<Tio, V>(dst + int64_t(j) * p.width, d);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive_relaxed(&empty[s]);
+    if (last) {
+      float sums[kAcc];
+#pragma unroll
+      for (int a = 0; a < kAcc; ++a) {
+        sums[a] = lane_sum(acc[a]);
+        acc[a] = make_float2(0.0f, 0.0f);
+      }
+      segment_reduce<true>(sums, s_acc, nthreads, ctid, nthreads, p, cb, cb - cb0, blockIdx.x,
+                           partial);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: validation, planning, dispatch.
 // ---------------------------------------------------------------------------
 
-constexpr int kUnroll = 4;
+#ifndef KAT_FWD_UNROLL
+#define KAT_FWD_UNROLL 4
+#endif
+#ifndef KAT_BWD_UNROLL
+#define KAT_BWD_UNROLL 2
+#endif
+constexpr int kUnroll = KAT_FWD_UNROLL;
+constexpr int kUnrollBwd = KAT_BWD_UNROLL;
 
 int elem_bytes(int dtype) { return dtype == KAT_DTYPE_F32 ? 4 : 2; }
 
@@ -778,23 +1258,23 @@ const void* bwd_kernel_for(int dtype, int vec) {
   switch (dtype) {
     case KAT_DTYPE_F32:
       switch (vec) {
-        case 4: return (const void*)kat_bwd_kernel<float, 4, kUnroll>;
-        case 2: return (const void*)kat_bwd_kernel<float, 2, kUnroll>;
-        default: return (const void*)kat_bwd_kernel<float, 1, kUnroll>;
+        case 4: return (const void*)kat_bwd_kernel<float, 4, kUnrollBwd>;
+        case 2: return (const void*)kat_bwd_kernel<float, 2, kUnrollBwd>;
+        default: return (const void*)kat_bwd_kernel<float, 1, kUnrollBwd>;
       }
     case KAT_DTYPE_F16:
       switch (vec) {
-        case 8: return (const void*)kat_bwd_kernel<__half, 8, kUnroll>;
-        case 4: return (const void*)kat_bwd_kernel<__half, 4, kUnroll>;
-        case 2: return (const void*)kat_bwd_kernel<__half, 2, kUnroll>;
-        default: return (const void*)kat_bwd_kernel<__half, 1, kUnroll>;
+        case 8: return (const void*)kat_bwd_kernel<__half, 8, kUnrollBwd>;
+        case 4: return (const void*)kat_bwd_kernel<__half, 4, kUnrollBwd>;
+        case 2: return (const void*)kat_bwd_kernel<__half, 2, kUnrollBwd>;
+        default: return (const void*)kat_bwd_kernel<__half, 1, kUnrollBwd>;
       }
     default:
       switch (vec) {
-        case 8: return (const void*)kat_bwd_kernel<__nv_bfloat16, 8, kUnroll>;
-        case 4: return (const void*)kat_bwd_kernel<__nv_bfloat16, 4, kUnroll>;
-        case 2: return (const void*)kat_bwd_kernel<__nv_bfloat16, 2, kUnroll>;
-        default: return (const void*)kat_bwd_kernel<__nv_bfloat16, 1, kUnroll>;
+        case 8: return (const void*)kat_bwd_kernel<__nv_bfloat16, 8, kUnrollBwd>;
+        case 4: return (const void*)kat_bwd_kernel<__nv_bfloat16, 4, kUnrollBwd>;
+        case 2: return (const void*)kat_bwd_kernel<__nv_bfloat16, 2, kUnrollBwd>;
+        default: return (const void*)kat_bwd_kernel<__nv_bfloat16, 1, kUnrollBwd>;
       }
   }
 }
@@ -840,7 +1320,7 @@ cudaError_t launch_fwd_t(const void* x, void* y, const float* num, const float* 
 template <typename Tio, int V>
 cudaError_t launch_bwd_t(const void* x, const void* gy, void* dx, const float* num,
                          const float* den, double* partial, const Plan& p, cudaStream_t s) {
-  kat_bwd_kernel<Tio, V, kUnroll><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
+  kat_bwd_kernel<Tio, V, kUnrollBwd><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
       static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num, den,
       partial, p);
   return cudaGetLastError();
@@ -887,6 +1367,253 @@ cudaError_t launch_bwd(int dtype, int vec, const void* x, const void* gy, void* 
   }
 }
 
+// ----- Bulk-copy pipeline: planning and launch --------------------------------
+
+constexpr int kPipeSmemBudget = 200 * 1024;
+
+// Tuning knobs (environment, read once): slot size per input tensor, ring depth cap and
+// largest single bulk copy.
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  if (e == nullptr || *e == 0) return dflt;
+  const long v = strtol(e, nullptr, 10);
+  return v > 0 ? int(v) : dflt;
+}
+int stage_target_bytes() {
+  static const int v = env_int("KAT_RATIONAL_STAGE_BYTES", 16 * 1024);
+  return v;
+}
+int max_stages() {
+  static const int v = std::min(env_int("KAT_RATIONAL_STAGES", 8), 8);
+  return v;
+}
+int poll_mode_ns() {
+  static const int v = [] {
+    const char* e = getenv("KAT_RATIONAL_POLL_NS");
+    return (e == nullptr || *e == 0) ? -1 : int(strtol(e, nullptr, 10));
+  }();
+  return v;
+}
+int tma_ctas_per_sm() {
+  static const int v = std::min(env_int("KAT_RATIONAL_TMA_CTAS", 1), 4);
+  return v;
+}
+uint32_t bulk_chunk_bytes() {
+  static const uint32_t v = uint32_t(env_int("KAT_RATIONAL_BULK_CHUNK", 1 << 20)) & ~15u;
+  return v < 16 ? 16 : v;
+}
+
+// KAT_RATIONAL_PIPELINE selects how 16-byte-vector problems stream their inputs (a
+// tuning switch; every choice computes the same results):
+//   unset / "async"  forward: register prefetch; backward: per-thread cp.async ring
+//   "registers"      register prefetch for both
+//   "bulk"           producer-warp cp.async.bulk ring for both
+int pipeline_mode() {
+  static const int mode = [] {
+    const char* e = getenv("KAT_RATIONAL_PIPELINE");
+    if (e != nullptr && strcmp(e, "registers") == 0) return 1;
+    if (e != nullptr && strcmp(e, "bulk") == 0) return 2;
+    return 0;
+  }();
+  return mode;
+}
+bool bulk_pipeline_enabled() { return pipeline_mode() == 2; }
+
+// Slot geometry for a plan made with 16-byte vectors.  Returns false when no ring of at
+// least two slots fits in shared memory.
+bool make_pipe(const Plan& p, int tensors, bool bwd, Pipe* q) {
+  if (p.items == 0) return false;
+  q->seg_bytes = p.tile_cols * 16;
+  const int64_t group_bytes = int64_t(q->seg_bytes) * p.tile_rows;
+  int64_t rows = stage_target_bytes() / group_bytes;
+  if (rows < 1) rows = 1;
+  q->stage_rows = int32_t(rows * p.tile_rows);
+  const int64_t acc_bytes = bwd ? int64_t(kAcc) * p.threads * 4 : 0;
+  const int64_t budget = kPipeSmemBudget / tma_ctas_per_sm() - kPipeHeader - acc_bytes;
+  int64_t stage_bytes = int64_t(q->stage_rows) * q->seg_bytes * tensors;
+  int64_t stages = budget / stage_bytes;
+  if (stages < 2) {
+    q->stage_rows = p.tile_rows;
+    stage_bytes = int64_t(q->stage_rows) * q->seg_bytes * tensors;
+    stages = budget / stage_bytes;
+    if (stages < 2) return false;
+  }
+  if (stages > max_stages()) stages = max_stages();
+  if (stage_bytes >= (1 << 20)) return false;  // mbarrier transaction-count range
+  q->stages = int32_t(stages);
+  q->contiguous = (p.col_blocks == 1 && int64_t(p.tile_cols) == p.vec_cols) ? 1 : 0;
+  q->smem_bytes = uint32_t(kPipeHeader + stages * stage_bytes + acc_bytes);
+  q->chunk_bytes = bulk_chunk_bytes();
+  q->poll_ns = poll_mode_ns();
+  return true;
+}
+
+std::map<std::pair<int, const void*>, bool> g_smem_attr;
+
+cudaError_t allow_dynamic_smem(int dev, const void* fn, uint32_t bytes) {
+  std::lock_guard<std::mutex> lock(g_cache_mu);
+  auto key = std::make_pair(dev, fn);
+  if (g_smem_attr.count(key)) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kPipeSmemBudget);
+  if (e != cudaSuccess) return e;
+  (void)bytes;
+  g_smem_attr[key] = true;
+  return cudaSuccess;
+}
+
+const void* fwd_tma_kernel_for(int dtype) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return (const void*)kat_fwd_tma_kernel<float>;
+    case KAT_DTYPE_F16: return (const void*)kat_fwd_tma_kernel<__half>;
+    default: return (const void*)kat_fwd_tma_kernel<__nv_bfloat16>;
+  }
+}
+
+const void* bwd_tma_kernel_for(int dtype) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return (const void*)kat_bwd_tma_kernel<float>;
+    case KAT_DTYPE_F16: return (const void*)kat_bwd_tma_kernel<__half>;
+    default: return (const void*)kat_bwd_tma_kernel<__nv_bfloat16>;
+  }
+}
+
+// Plan + slot geometry of the pipelined kernels (one block per SM).  Returns KAT_OK,
+// an error, or -1 when the pipelined kernels do not apply to this shape.
+int plan_tma(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
+             bool bwd, int* dev_out, Plan* p, Pipe* q) {
+  const int vmax = max_vec_for(dtype);
+  const int64_t gw = (channels / num_groups) * inner;
+  if (!bulk_pipeline_enabled() || gw % vmax != 0) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  int sms = 0;
+  if (device_sm_count(dev, &sms) != cudaSuccess) return KAT_ERR_CUDA;
+  const int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms,
+                                tma_ctas_per_sm(), p);
+  if (st != KAT_OK) return st;
+  if (!make_pipe(*p, bwd ? 2 : 1, bwd, q)) return -1;
+  *dev_out = dev;
+  return KAT_OK;
+}
+
+template <typename Tio>
+cudaError_t launch_fwd_tma_t(const void* x, void* y, const float* num, const float* den,
+                             const Plan& p, const Pipe& q, cudaStream_t s) {
+  kat_fwd_tma_kernel<Tio><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads + 32)),
+                            q.smem_bytes, s>>>(static_cast<const Tio*>(x), static_cast<Tio*>(y),
+                                               num, den, p, q);
+  return cudaGetLastError();
+}
+
+template <typename Tio>
+cudaError_t launch_bwd_tma_t(const void* x, const void* gy, void* dx, const float* num,
+                             const float* den, double* partial, const Plan& p, const Pipe& q,
+                             cudaStream_t s) {
+  kat_bwd_tma_kernel<Tio><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads + 32)),
+                            q.smem_bytes, s>>>(
+      static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num, den,
+      partial, p, q);
+  return cudaGetLastError();
+}
+
+#ifndef KAT_ASYNC_STAGES
+#define KAT_ASYNC_STAGES 4
+#endif
+#ifndef KAT_ASYNC_ROWS
+#define KAT_ASYNC_ROWS 2
+#endif
+constexpr int kAsyncStages = KAT_ASYNC_STAGES;
+constexpr int kAsyncRows = KAT_ASYNC_ROWS;
+
+size_t async_smem_bytes(int threads) {
+  return size_t(kAsyncStages) * kAsyncRows * 2 * 16 * threads + size_t(kAcc) * 4 * threads;
+}
+
+const void* bwd_async_kernel_for(int dtype) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return (const void*)kat_bwd_async_kernel<float, kAsyncStages, kAsyncRows>;
+    case KAT_DTYPE_F16: return (const void*)kat_bwd_async_kernel<__half, kAsyncStages, kAsyncRows>;
+    default: return (const void*)kat_bwd_async_kernel<__nv_bfloat16, kAsyncStages, kAsyncRows>;
+  }
+}
+
+// Plan of the cp.async backward: occupancy from the kernel's registers and its shared
+// memory at this block size.  Returns -1 when it does not apply.
+int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
+               int* dev_out, Plan* p) {
+  const int vmax = max_vec_for(dtype);
+  const int64_t gw = (channels / num_groups) * inner;
+  if (pipeline_mode() != 0 || gw % vmax != 0) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  int sms = 0;
+  if (device_sm_count(dev, &sms) != cudaSuccess) return KAT_ERR_CUDA;
+  Plan probe;
+  int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe);
+  if (st != KAT_OK) return st;
+  const void* fn = bwd_async_kernel_for(dtype);
+  const size_t smem = async_smem_bytes(probe.threads);
+  if (smem > size_t(kPipeSmemBudget)) return -1;
+  if (allow_dynamic_smem(dev, fn, uint32_t(smem)) != cudaSuccess) return KAT_ERR_CUDA;
+  int occ = 1;
+  {
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    auto key = std::make_tuple(dev, fn, probe.threads);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end()) {
+      occ = it->second;
+    } else {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, probe.threads, smem) !=
+          cudaSuccess)
+        return KAT_ERR_CUDA;
+      if (occ < 1) occ = 1;
+      g_occupancy[key] = occ;
+    }
+  }
+  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p);
+  *dev_out = dev;
+  return st;
+}
+
+template <typename Tio>
+cudaError_t launch_bwd_async_t(const void* x, const void* gy, void* dx, const float* num,
+                               const float* den, double* partial, const Plan& p, cudaStream_t s) {
+  kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows>
+      <<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), async_smem_bytes(p.threads), s>>>(
+          static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num,
+          den, partial, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bwd_async(int dtype, const void* x, const void* gy, void* dx, const float* num,
+                             const float* den, double* partial, const Plan& p, cudaStream_t s) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return launch_bwd_async_t<float>(x, gy, dx, num, den, partial, p, s);
+    case KAT_DTYPE_F16: return launch_bwd_async_t<__half>(x, gy, dx, num, den, partial, p, s);
+    default: return launch_bwd_async_t<__nv_bfloat16>(x, gy, dx, num, den, partial, p, s);
+  }
+}
+
+cudaError_t launch_fwd_tma(int dtype, const void* x, void* y, const float* num, const float* den,
+                           const Plan& p, const Pipe& q, cudaStream_t s) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return launch_fwd_tma_t<float>(x, y, num, den, p, q, s);
+    case KAT_DTYPE_F16: return launch_fwd_tma_t<__half>(x, y, num, den, p, q, s);
+    default: return launch_fwd_tma_t<__nv_bfloat16>(x, y, num, den, p, q, s);
+  }
+}
+
+cudaError_t launch_bwd_tma(int dtype, const void* x, const void* gy, void* dx, const float* num,
+                           const float* den, double* partial, const Plan& p, const Pipe& q,
+                           cudaStream_t s) {
+  switch (dtype) {
+    case KAT_DTYPE_F32: return launch_bwd_tma_t<float>(x, gy, dx, num, den, partial, p, q, s);
+    case KAT_DTYPE_F16: return launch_bwd_tma_t<__half>(x, gy, dx, num, den, partial, p, q, s);
+    default: return launch_bwd_tma_t<__nv_bfloat16>(x, gy, dx, num, den, partial, p, q, s);
+  }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -909,6 +1636,23 @@ const char* kat_rational_strerror(int status) {
 }
 
 int kat_rational_abi_version(void) { return KAT_RATIONAL_ABI_VERSION; }
+
+int kat_rational_device_status(int device, int reset, int* status) {
+  if (status == nullptr) return KAT_ERR_NULL_POINTER;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return KAT_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return KAT_ERR_CUDA;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_kat_status, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_kat_status, &zero, sizeof(int));
+  }
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return KAT_ERR_CUDA;
+  *status = v;
+  return KAT_OK;
+}
 
 int kat_rational_make_plan(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
                            int dtype, int vec, int sm_count, int ctas_per_sm,
@@ -935,6 +1679,20 @@ int kat_rational_fwd(const void* x, void* y, const float* numerator, const float
   const void* ptrs[2] = {x, y};
   const int vec = pick_vec(dtype, gw, ptrs, 2);
   Plan p;
+  if (vec == max_vec_for(dtype)) {
+    Pipe q;
+    int dev = 0;
+    st = plan_tma(batch, channels, inner, num_groups, dtype, false, &dev, &p, &q);
+    if (st != -1) {
+      if (st != KAT_OK) return st;
+      if (allow_dynamic_smem(dev, fwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      if (launch_fwd_tma(dtype, x, y, numerator, denominator, p, q,
+                         static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      return KAT_OK;
+    }
+  }
   st = plan_for_launch(fwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype, vec,
                        &p);
   if (st != KAT_OK) return st;
@@ -957,7 +1715,18 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
   if (device != prev && cudaSetDevice(device) != cudaSuccess) return KAT_ERR_CUDA;
   const int64_t gw = (channels / num_groups) * inner;
   uint64_t need = 0;
-  for (int vec = max_vec_for(dtype); vec >= 1; vec >>= 1) {
+  {
+    Plan p;
+    Pipe q;
+    int d = 0;
+    const int t = plan_tma(batch, channels, inner, num_groups, dtype, true, &d, &p, &q);
+    if (t == KAT_OK) need = p.workspace_bytes;
+    else if (t != -1) st = t;
+    const int a = st == KAT_OK ? plan_async(batch, channels, inner, num_groups, dtype, &d, &p) : -1;
+    if (a == KAT_OK) need = std::max<uint64_t>(need, p.workspace_bytes);
+    else if (a != -1) st = a;
+  }
+  for (int vec = max_vec_for(dtype); st == KAT_OK && vec >= 1; vec >>= 1) {
     if (gw % vec != 0) continue;
     Plan p;
     st = plan_for_launch(bwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype, vec,
@@ -986,7 +1755,47 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x, const fl
   const int64_t gw = (channels / num_groups) * inner;
   const void* ptrs[3] = {x, grad_out, grad_x};
   const int vec = n == 0 ? 1 : pick_vec(dtype, gw, ptrs, 3);
+  if (num_groups > 0x7fffffff) return KAT_ERR_BAD_GROUPS;
   Plan p;
+  if (n != 0 && vec == max_vec_for(dtype)) {
+    int dev = 0;
+    st = plan_async(batch, channels, inner, num_groups, dtype, &dev, &p);
+    if (st != -1) {
+      if (st != KAT_OK) return st;
+      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
+          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+        return KAT_ERR_WORKSPACE;
+      if (launch_bwd_async(dtype, x, grad_out, grad_x, numerator, denominator,
+                           static_cast<double*>(workspace), p, s) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
+          static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator,
+          p);
+      if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;
+      return KAT_OK;
+    }
+  }
+  if (n != 0 && vec == max_vec_for(dtype)) {
+    Pipe q;
+    int dev = 0;
+    st = plan_tma(batch, channels, inner, num_groups, dtype, true, &dev, &p, &q);
+    if (st != -1) {
+      if (st != KAT_OK) return st;
+      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
+          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+        return KAT_ERR_WORKSPACE;
+      if (allow_dynamic_smem(dev, bwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      if (launch_bwd_tma(dtype, x, grad_out, grad_x, numerator, denominator,
+                         static_cast<double*>(workspace), p, q, s) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
+          static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator,
+          p);
+      if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;
+      return KAT_OK;
+    }
+  }
   if (n == 0) {
     st = make_plan_impl(batch, channels, inner, num_groups, dtype, vec, 1, 1, &p);
   } else {
@@ -1002,7 +1811,6 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x, const fl
                    static_cast<double*>(workspace), p, s) != cudaSuccess)
       return KAT_ERR_CUDA;
   }
-  if (num_groups > 0x7fffffff) return KAT_ERR_BAD_GROUPS;
   kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
       static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator, p);
   if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;

@@ -31,7 +31,7 @@ def run_workload(w, device, on_gpu_inputs=False):
     with torch.no_grad():
         mod.weight_numerator.copy_(wn)
         mod.weight_denominator.copy_(wd)
-    xd = x.to(device).requires_grad_(True)
+    xd = x.detach().to(device).requires_grad_(True)
     y = mod(xd)
     y.backward(gy.to(device))
     torch.cuda.synchronize()
