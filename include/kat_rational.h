@@ -59,6 +59,7 @@ extern "C" {
 #define KAT_ERR_BAD_GROUPS 4        /* num_groups < 1 or channels % num_groups != 0 */
 #define KAT_ERR_WORKSPACE 5         /* workspace NULL or smaller than required */
 #define KAT_ERR_CUDA 6              /* CUDA runtime / launch error */
+#define KAT_ERR_SCRATCH_LIMIT 7     /* kat_rational_bwd_noalloc: problem exceeds its fixed scratch */
 
 /*
  * Forward: y = P(x)/Q(x).
@@ -95,6 +96,32 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x,
                      void* workspace, size_t workspace_bytes,
                      int64_t batch, int64_t channels, int64_t inner,
                      int64_t num_groups, int dtype, void* stream);
+
+/*
+ * Backward without any device allocation, for callers that cannot allocate where they run
+ * it: code inside a CUDA graph capture in the global capture mode (cudaMalloc is refused
+ * there), plugin hosts whose operator interface provides input/output buffers but no
+ * allocator, and fixed-budget real-time deployments where a mid-run cudaMalloc could stall
+ * the device or fail.  Same arguments and results as kat_rational_bwd minus the workspace:
+ * the partial sums go to a fixed 2 MiB file-scope device array instead, which every GPU
+ * that loads this library holds until the process exits.
+ *   - Problems whose backward needs more than 2 MiB of scratch
+ *     (kat_rational_bwd_workspace_size) are rejected with KAT_ERR_SCRATCH_LIMIT before
+ *     anything is enqueued.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress, with that device current) and caches it; make that first call
+ *     before any stream capture.  No call allocates (no cudaMalloc / cudaFree).
+ *   - Every call on a device shares the one array and leaves the last call's partial sums in
+ *     it; each call writes every entry it later reads, so nothing needs clearing.  Calls
+ *     that can overlap on the GPU (different streams, or different host threads) race on
+ *     the array: order them on one stream.
+ * No counterpart in the reference, whose backward allocates with torch.zeros in its launcher.
+ */
+int kat_rational_bwd_noalloc(const void* x, const void* grad_out, void* grad_x,
+                             const float* numerator, const float* denominator,
+                             float* grad_numerator, float* grad_denominator,
+                             int64_t batch, int64_t channels, int64_t inner,
+                             int64_t num_groups, int dtype, void* stream);
 
 /*
  * Bytes of workspace kat_rational_bwd needs for this problem on `device`

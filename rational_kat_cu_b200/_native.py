@@ -23,6 +23,7 @@ KAT_ERR_BAD_SHAPE = 3
 KAT_ERR_BAD_GROUPS = 4
 KAT_ERR_WORKSPACE = 5
 KAT_ERR_CUDA = 6
+KAT_ERR_SCRATCH_LIMIT = 7
 
 # Every symbol include/kat_rational.h declares.
 EXPORTED_SYMBOLS = (
@@ -33,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "kat_rational_abi_version",
     "kat_rational_make_plan",
     "kat_rational_device_status",
+    "kat_rational_bwd_noalloc",
 )
 
 ABI_VERSION = 1
@@ -98,6 +100,9 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_make_plan.restype = i32
     lib.kat_rational_device_status.argtypes = [i32, i32, ctypes.POINTER(ctypes.c_int)]
     lib.kat_rational_device_status.restype = i32
+    lib.kat_rational_bwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64,
+                                             i32, vp]
+    lib.kat_rational_bwd_noalloc.restype = i32
 
 
 def lib() -> ctypes.CDLL:

@@ -1631,6 +1631,9 @@ const char* kat_rational_strerror(int status) {
     case KAT_ERR_BAD_GROUPS: return "num_groups must be >= 1 and divide channels";
     case KAT_ERR_WORKSPACE: return "workspace is NULL, misaligned or smaller than required";
     case KAT_ERR_CUDA: return "CUDA runtime or kernel launch error";
+    case KAT_ERR_SCRATCH_LIMIT:
+      return "problem needs more backward scratch than kat_rational_bwd_noalloc's fixed "
+             "2 MiB device buffer holds; use kat_rational_bwd with a caller-allocated workspace";
     default: return "unknown kat_rational status";
   }
 }
@@ -1818,3 +1821,65 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x, const fl
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Backward without allocation.
+//
+// kat_rational_bwd needs a caller-allocated workspace for its per-block partial sums.  Some
+// callers cannot allocate device memory where they run the backward: code inside a CUDA
+// graph capture in the global capture mode (where cudaMalloc is refused), plugin hosts whose
+// operator interface hands over input/output buffers but no allocator, and fixed-budget
+// real-time deployments where a mid-run cudaMalloc may stall the device or fail.  For them,
+// kat_rational_bwd_noalloc uses a fixed file-scope device array as that workspace.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB on every device in use
+
+// The workspace of kat_rational_bwd_noalloc.  In host code this name only stands in for
+// the device symbol; its device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) double g_noalloc_scratch[kNoAllocScratchBytes / sizeof(double)];
+
+std::mutex g_noalloc_mu;
+std::map<int, void*> g_noalloc_addr;
+
+// Device address of the scratch array on `dev`, which must be the current device; looked up
+// once per device and cached.
+cudaError_t noalloc_scratch_address(int dev, void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  auto it = g_noalloc_addr.find(dev);
+  if (it != g_noalloc_addr.end()) {
+    *out = it->second;
+    return cudaSuccess;
+  }
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) return e;
+  g_noalloc_addr[dev] = ptr;
+  *out = ptr;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int kat_rational_bwd_noalloc(const void* x, const void* grad_out, void* grad_x,
+                                        const float* numerator, const float* denominator,
+                                        float* grad_numerator, float* grad_denominator,
+                                        int64_t batch, int64_t channels, int64_t inner,
+                                        int64_t num_groups, int dtype, void* stream) {
+  int64_t n = 0;
+  int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
+  if (st != KAT_OK) return st;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  size_t need = 0;
+  st = kat_rational_bwd_workspace_size(batch, channels, inner, num_groups, dtype, dev, &need);
+  if (st != KAT_OK) return st;
+  if (need > kNoAllocScratchBytes) return KAT_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  if (noalloc_scratch_address(dev, &scratch) != cudaSuccess) return KAT_ERR_CUDA;
+  return kat_rational_bwd(x, grad_out, grad_x, numerator, denominator, grad_numerator,
+                          grad_denominator, scratch, kNoAllocScratchBytes, batch, channels, inner,
+                          num_groups, dtype, stream);
+}
