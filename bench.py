@@ -54,7 +54,9 @@ def parse_args():
     ap.add_argument("--workload", default="kat_group_vitb_bf16")
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of a CUDA graph")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--kernel-iters", type=int, default=50)
+    ap.add_argument("--e2e-chunks", type=int, default=16,
+                    help="row chunks the host-buffer pipeline overlaps")
+    ap.add_argument("--kernel-iters", type=int, default=100)
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU budget of the reference-path baseline")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
@@ -328,60 +330,82 @@ def run_ours(args):
     ms_per_step = ms_total / args.steps
     value = world * N / (ms_per_step * 1e-3) / 1e9
 
-    # Kernel-level timing of the forward and the fused backward (C ABI calls, device-resident
-    # inputs), per launch with CUDA events on the launching stream.
-    n_rep = wn.repeat(w.groups, 1).to(dev)
-    d_rep = wd.to(dev)
+    # Kernel-level timing: back-to-back C-ABI launches on device-resident, preallocated
+    # buffers (no Python work inside the loop beyond the call), CUDA events on the launching
+    # stream around the whole run, average per launch.
+    import ctypes
+
+    from rational_kat_cu_b200 import _native
+
+    lib = _native.lib()
+    code = {"f32": _native.KAT_DTYPE_F32, "bf16": _native.KAT_DTYPE_BF16,
+            "f16": _native.KAT_DTYPE_F16}[w.dtype]
+    dims = w.dims()
+    n_rep = wn.repeat(w.groups, 1).to(dev).contiguous()
+    d_rep = wd.to(dev).contiguous()
     xs = x.detach()
-    fwd_fn = kat.rational_fwd_cuda_2d if w.layout == "nchw" else kat.rational_fwd_cuda
-    bwd_fn = kat.rational_bwd_cuda_2d if w.layout == "nchw" else kat.rational_bwd_cuda
+    y_buf = torch.empty_like(xs)
+    dx_buf = torch.empty_like(xs)
+    dn_buf = torch.empty(w.groups, 6, device=dev)
+    dd_buf = torch.empty(w.groups, 4, device=dev)
+    ws_need = ctypes.c_size_t(0)
+    _native.check("workspace", lib.kat_rational_bwd_workspace_size(
+        dims[0], dims[1], dims[2], w.groups, code, dev.index, ctypes.byref(ws_need)))
+    ws_buf = torch.empty(max(ws_need.value, 16), dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    fwd_args = (xs.data_ptr(), y_buf.data_ptr(), n_rep.data_ptr(), d_rep.data_ptr(),
+                dims[0], dims[1], dims[2], w.groups, code, sp)
+    bwd_args = (xs.data_ptr(), gy.data_ptr(), dx_buf.data_ptr(), n_rep.data_ptr(),
+                d_rep.data_ptr(), dn_buf.data_ptr(), dd_buf.data_ptr(), ws_buf.data_ptr(),
+                ws_buf.numel(), dims[0], dims[1], dims[2], w.groups, code, sp)
 
-    def time_launches(fn, iters):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(iters)]
+    def time_launches(fn, args, iters):
         for _ in range(3):
-            fn()
+            _native.check("launch", fn(*args))
         torch.cuda.synchronize(dev)
-        for a, b in evs:
-            a.record(stream)
-            fn()
-            b.record(stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(iters):
+            fn(*args)
+        b.record(stream)
         torch.cuda.synchronize(dev)
-        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+        return a.elapsed_time(b) / iters
 
-    fwd_ms = time_launches(lambda: fwd_fn(xs, n_rep, d_rep, w.groups), args.kernel_iters)
-    bwd_ms = time_launches(lambda: bwd_fn(gy, xs, n_rep, d_rep, w.groups), args.kernel_iters)
+    fwd_ms = time_launches(lib.kat_rational_fwd, fwd_args, args.kernel_iters)
+    bwd_ms = time_launches(lib.kat_rational_bwd, bwd_args, args.kernel_iters)
     mode = os.environ.get("KAT_RATIONAL_PIPELINE", "async")
     bwd_kernel_name = {"registers": "kat_bwd_kernel", "bulk": "kat_bwd_tma_kernel"}.get(
         mode, "kat_bwd_async_kernel") + " + kat_bwd_reduce_kernel (one C-ABI backward call)"
     fwd_gbs = 2 * N * elem_bytes / (fwd_ms * 1e-3) / 1e9
     bwd_gbs = 3 * N * elem_bytes / (bwd_ms * 1e-3) / 1e9
 
-    # End to end through the module with host buffers.
+    # End to end through the public host-buffer API: pinned host x, grad_out in; y, dx and
+    # the coefficient gradients back in pinned host memory, copies overlapped with compute.
+    from rational_kat_cu_b200.host_io import HostPipeline
+
     h_x = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
     h_gy = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
     h_x.copy_(xs.cpu())
     h_gy.copy_(gy.cpu())
     h_y = torch.empty_like(h_x, pin_memory=True)
     h_dx = torch.empty_like(h_x, pin_memory=True)
-    h_dn = torch.empty(mod.weight_numerator.shape, pin_memory=True)
-    h_dd = torch.empty(mod.weight_denominator.shape, pin_memory=True)
+    h_grads = [torch.empty(mod.weight_numerator.shape, pin_memory=True),
+               torch.empty(mod.weight_denominator.shape, pin_memory=True)]
+    pipe = HostPipeline(mod, chunks=args.e2e_chunks)
 
     def e2e_step():
-        xd = h_x.to(dev, non_blocking=True).requires_grad_(True)
-        gd = h_gy.to(dev, non_blocking=True)
         mod.zero_grad(set_to_none=True)
-        y = mod(xd)
-        y.backward(gd)
         if dist is not None:
+            pipe.run(h_x, h_gy, h_y, h_dx)
             kdist.allreduce_coefficient_grads(mod)
-        h_y.copy_(y.detach(), non_blocking=True)
-        h_dx.copy_(xd.grad, non_blocking=True)
-        h_dn.copy_(mod.weight_numerator.grad, non_blocking=True)
-        h_dd.copy_(mod.weight_denominator.grad, non_blocking=True)
+            h_grads[0].copy_(mod.weight_numerator.grad, non_blocking=True)
+            h_grads[1].copy_(mod.weight_denominator.grad, non_blocking=True)
+        else:
+            pipe.run(h_x, h_gy, h_y, h_dx, grads_host=h_grads, wait=False)
 
     for _ in range(2):
         e2e_step()
+    pipe.wait()
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
@@ -389,6 +413,7 @@ def run_ours(args):
     e_start.record(stream)
     for _ in range(args.e2e_steps):
         e2e_step()
+    pipe.wait()
     e_end.record(stream)
     torch.cuda.synchronize(dev)
     e_ms = e_start.elapsed_time(e_end)
@@ -399,7 +424,7 @@ def run_ours(args):
     e2e_ms_step = e_ms / args.e2e_steps
     e2e_value = world * N / (e2e_ms_step * 1e-3) / 1e9
     h2d = 2 * N * elem_bytes
-    d2h = 2 * N * elem_bytes + (h_dn.numel() + h_dd.numel()) * 4
+    d2h = 2 * N * elem_bytes + sum(h.numel() for h in h_grads) * 4
 
     clocks = None
     if sampler:
@@ -444,7 +469,10 @@ def run_ours(args):
                 "step_hbm_frac": step_bytes * world / (ms_per_step * 1e-3) / 1e9 / (peak * world),
             },
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms_step},
+                    "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms_step,
+                    "api": f"rational_kat_cu_b200.host_io.HostPipeline ({args.e2e_chunks} "
+                           f"row chunks, H2D / compute / D2H overlapped, consecutive steps "
+                           f"overlapped)"},
             "gpu_launches": 3 * args.steps * world,
             "cpu_baseline": cpu,
             "clocks": clocks,

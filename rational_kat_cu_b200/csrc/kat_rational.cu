@@ -642,8 +642,17 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+#ifndef KAT_ASYNC_MAXNREG
+#define KAT_ASYNC_MAXNREG 0
+#endif
+#if KAT_ASYNC_MAXNREG > 0
+#define KAT_ASYNC_BOUNDS __maxnreg__(KAT_ASYNC_MAXNREG)
+#else
+#define KAT_ASYNC_BOUNDS __launch_bounds__(kMaxThreads)
+#endif
+
 template <typename Tio, int kStages, int kRows>
-__global__ void __launch_bounds__(kMaxThreads)
+__global__ void KAT_ASYNC_BOUNDS
 kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
                      const float* __restrict__ num, const float* __restrict__ den,
                      double* __restrict__ partial, const Plan p) {
@@ -1115,7 +1124,7 @@ int validate_dims(int64_t batch, int64_t channels, int64_t inner, int64_t num_gr
 int max_vec_for(int dtype) { return 16 / elem_bytes(dtype); }
 
 int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-                   int vec, int sm_count, int ctas_per_sm, Plan* p) {
+                   int vec, int sm_count, int ctas_per_sm, Plan* p, int max_cols = kMaxThreads) {
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
@@ -1141,17 +1150,17 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
     p->tile_rows = 1;
     return KAT_OK;
   }
-  if (p->vec_cols <= kMaxThreads) {
+  if (p->vec_cols <= max_cols) {
     p->tile_cols = int32_t(p->vec_cols);
-    int64_t tr = kMaxThreads / p->tile_cols;
+    int64_t tr = max_cols / p->tile_cols;
     if (tr > batch) tr = batch;
     if (tr < 1) tr = 1;
     p->tile_rows = int32_t(tr);
   } else {
-    const int64_t ncb = (p->vec_cols + kMaxThreads - 1) / kMaxThreads;
+    const int64_t ncb = (p->vec_cols + max_cols - 1) / max_cols;
     int64_t tcols = (p->vec_cols + ncb - 1) / ncb;
     tcols = (tcols + 31) / 32 * 32;
-    if (tcols > kMaxThreads) tcols = kMaxThreads;
+    if (tcols > max_cols) tcols = max_cols;
     p->tile_cols = int32_t(tcols);
     p->tile_rows = 1;
   }
@@ -1549,8 +1558,11 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
   int sms = 0;
   if (device_sm_count(dev, &sms) != cudaSuccess) return KAT_ERR_CUDA;
+  static const int max_cols = std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kMaxThreads),
+                                        kMaxThreads) / 32 * 32;
   Plan probe;
-  int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe);
+  int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
+                          std::max(32, max_cols));
   if (st != KAT_OK) return st;
   const void* fn = bwd_async_kernel_for(dtype);
   const size_t smem = async_smem_bytes(probe.threads);
@@ -1571,7 +1583,8 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
       g_occupancy[key] = occ;
     }
   }
-  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p);
+  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p,
+                      std::max(32, max_cols));
   *dev_out = dev;
   return st;
 }
