@@ -266,6 +266,10 @@ def run_ours(args):
     with torch.no_grad():
         mod.weight_numerator.copy_(wn)
         mod.weight_denominator.copy_(wd)
+    if dist is not None:
+        # Coefficient gradients are exchanged inside the backward's reduction kernel over
+        # NVLink peer memory (no NCCL call on the step).
+        mod.enable_data_parallel(timeout_ms=20000)
     x, gy = w.inputs(dev)
     x.requires_grad_(True)
     stream = torch.cuda.current_stream(dev)
@@ -302,8 +306,6 @@ def run_ours(args):
             mod.zero_grad(set_to_none=True)
             x.grad = None
             step_eager()
-        if dist is not None:
-            kdist.allreduce_coefficient_grads(mod)
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
@@ -454,7 +456,8 @@ def run_ours(args):
                 "l2": f"inputs larger than L2 ({N * elem_bytes / 1e6:.0f} MB per tensor > "
                       f"{L2_BYTES / 1e6:.0f} MB)",
                 "step": "module forward + backward" + (" in a CUDA graph" if graph else "")
-                        + (" + NCCL coefficient-gradient all-gather" if world > 1 else ""),
+                        + (" with the coefficient-gradient exchange fused into the reduction "
+                           "kernel (NVLink peer stores)" if world > 1 else ""),
             },
             "roofline": {
                 "bound": "hbm", "kernel": bwd_kernel_name,

@@ -142,6 +142,58 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
 #define KAT_DEVICE_WAIT_TIMEOUT 1
 int kat_rational_device_status(int device, int reset, int* status);
 
+/*
+ * Data-parallel backward: kat_rational_bwd whose coefficient gradients are, in the same
+ * call, exchanged with every other rank over NVLink peer memory and added in rank order
+ * (optionally averaged), so every rank ends with the same bit-identical gradients.  grad_x
+ * stays local.  `peers` describes the ranks of one node: buffers[r] is rank r's exchange
+ * buffer (kat_rational_exchange_buffer_bytes(num_groups) bytes, 16-byte aligned,
+ * zero-filled once before the first call) as mapped into this process (peer access or IPC);
+ * buffers[rank] is this rank's own.  Every rank must make the same sequence of calls: the
+ * k-th call of each rank pairs with the k-th call of the others.  A rank that does not
+ * arrive within timeout_ms makes the others set KAT_DEVICE_EXCHANGE_TIMEOUT in the device
+ * status word and write NaN gradients (the kernel returns; the context stays usable).
+ * Replaces the reference's (absent) distributed layer; no counterpart there.
+ */
+#define KAT_MAX_PEERS 8
+#define KAT_DEVICE_EXCHANGE_TIMEOUT 2
+typedef struct kat_rational_peers {
+  int32_t world_size;               /* 1 .. KAT_MAX_PEERS */
+  int32_t rank;                     /* this process's rank */
+  int32_t average;                  /* nonzero: divide the sum by world_size */
+  int32_t timeout_ms;               /* bound on the wait for the other ranks */
+  void* buffers[KAT_MAX_PEERS];     /* every rank's exchange buffer, mapped here */
+} kat_rational_peers;
+
+size_t kat_rational_exchange_buffer_bytes(int64_t num_groups);
+
+/* Let kernels on `device` access memory of `peer_device` (NVLink peer access; idempotent). */
+int kat_rational_enable_peer_access(int device, int peer_device);
+
+/*
+ * Exchange-buffer set-up for kat_rational_bwd_allreduce across processes (one per GPU),
+ * outside the per-step path (these calls allocate / map memory and synchronise):
+ *   create   cudaMalloc a zeroed local buffer of kat_rational_exchange_buffer_bytes(G) on the
+ *            current device and write its 64-byte CUDA IPC handle to `ipc_handle`;
+ *   open     map a peer's buffer from its handle on the current device (lazy peer access),
+ *            then check it is reachable (pointer attributes + a 16-byte copy into the
+ *            caller's 16-byte `local_probe` device buffer) — an unreachable mapping is an
+ *            error here, never a kernel fault later;
+ *   close / destroy  undo open / create.
+ */
+int kat_rational_exchange_create(int64_t num_groups, void** buffer, void* ipc_handle);
+int kat_rational_exchange_open(const void* ipc_handle, void* local_probe, void** peer_buffer);
+int kat_rational_exchange_close(void* peer_buffer);
+int kat_rational_exchange_destroy(void* buffer);
+
+int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x,
+                               const float* numerator, const float* denominator,
+                               float* grad_numerator, float* grad_denominator,
+                               void* workspace, size_t workspace_bytes,
+                               int64_t batch, int64_t channels, int64_t inner,
+                               int64_t num_groups, int dtype,
+                               const kat_rational_peers* peers, void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* kat_rational_strerror(int status);
 

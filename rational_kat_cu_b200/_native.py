@@ -35,7 +35,30 @@ EXPORTED_SYMBOLS = (
     "kat_rational_make_plan",
     "kat_rational_device_status",
     "kat_rational_bwd_noalloc",
+    "kat_rational_exchange_buffer_bytes",
+    "kat_rational_bwd_allreduce",
+    "kat_rational_enable_peer_access",
+    "kat_rational_exchange_create",
+    "kat_rational_exchange_open",
+    "kat_rational_exchange_close",
+    "kat_rational_exchange_destroy",
 )
+
+KAT_MAX_PEERS = 8
+KAT_DEVICE_WAIT_TIMEOUT = 1
+KAT_DEVICE_EXCHANGE_TIMEOUT = 2
+
+
+class KatPeers(ctypes.Structure):
+    """Mirror of `kat_rational_peers`."""
+
+    _fields_ = [
+        ("world_size", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("average", ctypes.c_int32),
+        ("timeout_ms", ctypes.c_int32),
+        ("buffers", ctypes.c_void_p * KAT_MAX_PEERS),
+    ]
 
 ABI_VERSION = 1
 
@@ -103,6 +126,22 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_bwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, i64,
                                              i32, vp]
     lib.kat_rational_bwd_noalloc.restype = i32
+    lib.kat_rational_exchange_buffer_bytes.argtypes = [i64]
+    lib.kat_rational_exchange_buffer_bytes.restype = ctypes.c_size_t
+    lib.kat_rational_bwd_allreduce.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_size_t,
+                                               i64, i64, i64, i64, i32, ctypes.POINTER(KatPeers),
+                                               vp]
+    lib.kat_rational_bwd_allreduce.restype = i32
+    lib.kat_rational_enable_peer_access.argtypes = [i32, i32]
+    lib.kat_rational_enable_peer_access.restype = i32
+    lib.kat_rational_exchange_create.argtypes = [i64, ctypes.POINTER(ctypes.c_void_p), vp]
+    lib.kat_rational_exchange_create.restype = i32
+    lib.kat_rational_exchange_open.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_void_p)]
+    lib.kat_rational_exchange_open.restype = i32
+    lib.kat_rational_exchange_close.argtypes = [vp]
+    lib.kat_rational_exchange_close.restype = i32
+    lib.kat_rational_exchange_destroy.argtypes = [vp]
+    lib.kat_rational_exchange_destroy.restype = i32
 
 
 def lib() -> ctypes.CDLL:

@@ -74,7 +74,33 @@ struct Plan {
   int32_t max_segments;
   int32_t max_local_groups;
   uint64_t workspace_bytes;
+  int64_t items_q;     // items per block, floor(items / blocks)
+  int64_t items_r;     // the first items_r blocks take one more item
+  uint64_t rows_m;     // multiply-shift constants for dividing by rows ...
+  uint64_t vg_m;       // ... and by vec_group
+  int32_t rows_s1, rows_s2, vg_s1, vg_s2;
 };
+
+// Division by an invariant divisor d >= 1 with a multiply and shifts (Granlund and
+// Montgomery, "Division by invariant integers using multiplication", PLDI 1994, the
+// round-up method of their Figure 4.1 for N = 64): with l = ceil(log2 d),
+// m = floor(2^64 (2^l - d) / d) + 1, sh1 = min(l, 1), sh2 = max(l - 1, 0):
+//   t = mulhi(m, n);  n / d = (t + ((n - t) >> sh1)) >> sh2   for all 0 <= n < 2^64.
+void make_divider(uint64_t d, uint64_t* m, int32_t* s1, int32_t* s2) {
+  int l = 0;
+  while (l < 64 && (uint64_t(1) << l) < d) ++l;
+  const unsigned __int128 two64 = (unsigned __int128)1 << 64;
+  const unsigned __int128 num = two64 * (((unsigned __int128)1 << l) - d);
+  *m = uint64_t(num / d + 1);
+  *s1 = l < 1 ? l : 1;
+  *s2 = l - 1 > 0 ? l - 1 : 0;
+}
+
+__device__ __forceinline__ int64_t fast_div(int64_t n, uint64_t m, int32_t s1, int32_t s2) {
+  const uint64_t un = uint64_t(n);
+  const uint64_t t = __umul64hi(m, un);
+  return int64_t((t + ((un - t) >> s1)) >> s2);
+}
 
 // ---------------------------------------------------------------------------
 // Element I/O: a vector of V elements <-> float[V].
@@ -415,8 +441,8 @@ __device__ __forceinline__ typename RawOf<Tio, V>::T bwd_vec(typename RawOf<Tio,
 
 // Item range [i0, i1) of block `blk` (even split, sizes differ by at most one).
 __device__ __forceinline__ void block_items(const Plan& p, int64_t blk, int64_t& i0, int64_t& i1) {
-  i0 = p.items * blk / p.blocks;
-  i1 = p.items * (blk + 1) / p.blocks;
+  i0 = blk * p.items_q + min(blk, p.items_r);
+  i1 = i0 + p.items_q + (blk < p.items_r ? 1 : 0);
 }
 
 // Per-block, per-group reduction of one segment's per-thread sums (fixed order):
@@ -742,43 +768,69 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
   }
 }
 
-// Grid reduction: one block per group, warp k sums coefficient slot k over all
-// blocks in block order (lane j takes blocks j, j+32, ...; fixed xor tree).
-__global__ void __launch_bounds__(kReduceThreads)
-kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restrict__ den,
-                      float* __restrict__ dnum, float* __restrict__ dden, const Plan p) {
-  const int64_t g = blockIdx.x;
-  const int k = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  double s = 0.0;
+// Sum of group g's 10 coefficient slots over all blocks of the grid, computed by one warp:
+// lane j takes blocks j, j+32, ... in order (each block's segments in order), then the 10
+// lane totals are added with a fixed xor tree, leaving the result in every lane.
+__device__ __forceinline__ void group_totals(const double* __restrict__ partial, const Plan& p,
+                                             int64_t g, int lane, double (&tot)[kAcc]) {
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k) tot[k] = 0.0;
   for (int64_t blk = lane; blk < p.blocks; blk += 32) {
     int64_t i0, i1;
     block_items(p, blk, i0, i1);
-    const int64_t cb0 = i0 / p.rows;
-    const int64_t cb1 = (i1 - 1) / p.rows;
+    const int64_t cb0 = fast_div(i0, p.rows_m, p.rows_s1, p.rows_s2);
+    const int64_t cb1 = fast_div(i1 - 1, p.rows_m, p.rows_s1, p.rows_s2);
     for (int64_t cb = cb0; cb <= cb1; ++cb) {
       const int64_t col0 = cb * p.tile_cols;
       const int64_t col_end = min(col0 + p.tile_cols, p.vec_cols);
-      const int64_t g_first = col0 / p.vec_group;
-      const int64_t g_last = (col_end - 1) / p.vec_group;
+      const int64_t g_first = fast_div(col0, p.vg_m, p.vg_s1, p.vg_s2);
+      const int64_t g_last = fast_div(col_end - 1, p.vg_m, p.vg_s1, p.vg_s2);
       if (g < g_first) break;
       if (g > g_last) continue;
-      s += partial[((blk * p.max_segments + (cb - cb0)) * p.max_local_groups + (g - g_first)) * kAcc + k];
+      const double* src =
+          partial + ((blk * p.max_segments + (cb - cb0)) * p.max_local_groups + (g - g_first)) * kAcc;
+#pragma unroll
+      for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
     }
   }
 #pragma unroll
-  for (int m = 16; m > 0; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
-  if (lane == 0) {
-    const float v = float(s);
-    if (k < 6) {
-      dnum[g * 6 + k] = v;
-    } else {
-      const float b = den[g * 4 + (k - 6)];
-      // sgn(b) with sgn(0) = 0 and sgn(NaN) = NaN, as torch.sgn.
-      const float sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
-      dden[g * 4 + (k - 6)] = -(sg * v);
-    }
+  for (int k = 0; k < kAcc; ++k) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) tot[k] += __shfl_xor_sync(0xffffffffu, tot[k], m);
   }
+}
+
+// Writes one group's gradients from its totals: d_num = sums, d_den = -sgn(b) * sums (with
+// sgn(0) = 0 and sgn(NaN) = NaN, as torch.sgn).  Lane k < 10 writes slot k.
+__device__ __forceinline__ void write_group(const double (&tot)[kAcc], double scale, bool ok,
+                                            int64_t g, int lane, const float* __restrict__ den,
+                                            float* __restrict__ dnum, float* __restrict__ dden) {
+  double v = 0.0;
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k)
+    if (lane == k) v = tot[k];
+  if (lane >= kAcc) return;
+  const float f = ok ? float(v * scale) : __int_as_float(0x7fc00000);
+  if (lane < 6) {
+    dnum[g * 6 + lane] = f;
+  } else {
+    const float b = den[g * 4 + (lane - 6)];
+    const float sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
+    dden[g * 4 + (lane - 6)] = -(sg * f);
+  }
+}
+
+// Grid reduction: one warp per group.
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(kReduceWarps * 32)
+kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restrict__ den,
+                      float* __restrict__ dnum, float* __restrict__ dden, const Plan p) {
+  const int64_t g = int64_t(blockIdx.x) * kReduceWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (g >= p.num_groups) return;
+  double tot[kAcc];
+  group_totals(partial, p, g, lane, tot);
+  write_group(tot, 1.0, true, g, lane, den, dnum, dden);
 }
 
 // ---------------------------------------------------------------------------
@@ -1094,6 +1146,124 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
 }
 
 // ---------------------------------------------------------------------------
+// Grid reduction fused with the cross-GPU exchange (data parallel over NVLink).
+//
+// One block: (1) sums every (group, slot) over the blocks of this GPU exactly as
+// kat_bwd_reduce_kernel does; (2) stores the G x 10 fp64 sums into every rank's exchange
+// buffer (peer memory, NVLink stores), into the row of this rank in the half selected by
+// the call's epoch parity; (3) raises this rank's flag on every rank (system-scope
+// release after a system fence); (4) waits, bounded by a wall-clock limit, until every
+// rank's flag on this GPU reached the epoch (system-scope acquire); (5) adds the ranks in
+// rank order in fp64 (optionally divided by the world size) and writes d_num / d_den.  All
+// ranks add the same numbers in the same order, so their gradients are bit-identical.
+// The epoch is a per-buffer counter the kernel increments, so calls must be made the same
+// number of times on every rank (each rank's k-th call pairs with every other rank's k-th
+// call).  Two epoch halves let a rank run ahead by one call without overwriting data a
+// peer still reads.  A wait that runs out sets KAT_DEVICE_EXCHANGE_TIMEOUT in the device
+// status word and writes NaN gradients.
+//
+// Exchange buffer layout (every rank, zero-initialised once):
+//   [0]    u64 epoch                        [64]  u64 flags[kMaxPeers] (flag[src] = epoch)
+//   [128]  f64 inbox[2][kMaxPeers][G][10]
+// ---------------------------------------------------------------------------
+
+constexpr int kMaxPeers = 8;
+constexpr size_t kExchangeHeader = 128;
+constexpr int kStatusExchangeTimeout = 2;
+
+struct Peers {
+  int32_t world;
+  int32_t rank;
+  int32_t average;
+  int32_t timeout_ms;
+  char* buf[kMaxPeers];
+};
+
+__device__ __forceinline__ void st_release_sys(uint64_t* ptr, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* ptr) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void __launch_bounds__(kReduceThreads, 1)
+kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* __restrict__ den,
+                               float* __restrict__ dnum, float* __restrict__ dden, const Plan p,
+                               const Peers peers) {
+  extern __shared__ double s_sum[];   // [G * 10]
+  __shared__ uint64_t s_epoch;
+  __shared__ int s_ok;
+  const int G = int(p.num_groups);
+  const int n_out = G * kAcc;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int g = warp; g < G; g += nwarps) {
+    double tot[kAcc];
+    group_totals(partial, p, g, lane, tot);
+#pragma unroll
+    for (int k = 0; k < kAcc; ++k)
+      if (lane == k) s_sum[g * kAcc + k] = tot[k];
+  }
+  if (tid == 0) {
+    uint64_t* ep = reinterpret_cast<uint64_t*>(peers.buf[peers.rank]);
+    s_epoch = *ep + 1;
+    *ep = s_epoch;
+  }
+  __syncthreads();
+  const uint64_t epoch = s_epoch;
+  const size_t half = size_t(epoch & 1u) * kMaxPeers;
+  for (int r = 0; r < peers.world; ++r) {
+    double* dst = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader) +
+                  (half + size_t(peers.rank)) * size_t(n_out);
+    for (int i = tid; i < n_out; i += blockDim.x) dst[i] = s_sum[i];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();
+    for (int r = 0; r < peers.world; ++r)
+      st_release_sys(reinterpret_cast<uint64_t*>(peers.buf[r] + 64) + peers.rank, epoch);
+    const uint64_t* flags = reinterpret_cast<const uint64_t*>(peers.buf[peers.rank] + 64);
+    const uint64_t limit = uint64_t(peers.timeout_ms) * 1000000ull;
+    const uint64_t t0 = global_timer_ns();
+    int ok = 1;
+    for (int q = 0; q < peers.world && ok; ++q) {
+      while (ld_acquire_sys(flags + q) < epoch) {
+        if (global_timer_ns() - t0 > limit) {
+          ok = 0;
+          atomicExch(&g_kat_status, kStatusExchangeTimeout);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  const double* inbox = reinterpret_cast<const double*>(peers.buf[peers.rank] + kExchangeHeader) +
+                        half * size_t(n_out);
+  const double scale = peers.average ? 1.0 / double(peers.world) : 1.0;
+  for (int g = warp; g < G; g += nwarps) {
+    double tot[kAcc];
+#pragma unroll
+    for (int k = 0; k < kAcc; ++k) {
+      double v = 0.0;
+      for (int q = 0; q < peers.world; ++q) v += inbox[size_t(q) * n_out + g * kAcc + k];
+      tot[k] = v;
+    }
+    write_group(tot, scale, s_ok != 0, g, lane, den, dnum, dden);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side: validation, planning, dispatch.
 // ---------------------------------------------------------------------------
 
@@ -1180,6 +1350,10 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   if (lg > num_groups) lg = num_groups;
   p->max_local_groups = int32_t(lg);
   p->workspace_bytes = uint64_t(blocks) * uint64_t(segs) * uint64_t(lg) * kAcc * sizeof(double);
+  p->items_q = p->items / blocks;
+  p->items_r = p->items % blocks;
+  make_divider(uint64_t(batch), &p->rows_m, &p->rows_s1, &p->rows_s2);
+  make_divider(uint64_t(p->vec_group), &p->vg_m, &p->vg_s1, &p->vg_s2);
   return KAT_OK;
 }
 
@@ -1627,6 +1801,95 @@ cudaError_t launch_bwd_tma(int dtype, const void* x, const void* gy, void* dx, c
   }
 }
 
+int launch_reduce(const void* workspace, const float* den, float* dnum, float* dden,
+                  const Plan& p, const Peers* peers, cudaStream_t s) {
+  if (peers == nullptr) {
+    const unsigned grid = unsigned((p.num_groups + kReduceWarps - 1) / kReduceWarps);
+    kat_bwd_reduce_kernel<<<dim3(grid), dim3(kReduceWarps * 32), 0, s>>>(
+        static_cast<const double*>(workspace), den, dnum, dden, p);
+  } else {
+    const size_t smem = size_t(p.num_groups) * kAcc * sizeof(double);
+    if (smem > 48 * 1024) {
+      if (cudaFuncSetAttribute((const void*)kat_bwd_reduce_exchange_kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+          cudaSuccess)
+        return KAT_ERR_CUDA;
+    }
+    kat_bwd_reduce_exchange_kernel<<<1, dim3(kReduceThreads), smem, s>>>(
+        static_cast<const double*>(workspace), den, dnum, dden, p, *peers);
+  }
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+// The backward: the fused elementwise/partial-sum kernel chosen for the shape, then the grid
+// reduction — plain, or fused with the cross-GPU exchange when `peers` is given.
+int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* numerator,
+             const float* denominator, float* grad_numerator, float* grad_denominator,
+             void* workspace, size_t workspace_bytes, int64_t batch, int64_t channels,
+             int64_t inner, int64_t num_groups, int dtype, void* stream, const Peers* peers) {
+  int64_t n = 0;
+  int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
+  if (st != KAT_OK) return st;
+  if (numerator == nullptr || denominator == nullptr || grad_numerator == nullptr ||
+      grad_denominator == nullptr)
+    return KAT_ERR_NULL_POINTER;
+  if (n != 0 && (x == nullptr || grad_out == nullptr)) return KAT_ERR_NULL_POINTER;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t gw = (channels / num_groups) * inner;
+  const void* ptrs[3] = {x, grad_out, grad_x};
+  const int vec = n == 0 ? 1 : pick_vec(dtype, gw, ptrs, 3);
+  if (num_groups > 0x7fffffff) return KAT_ERR_BAD_GROUPS;
+  Plan p;
+  if (n != 0 && vec == max_vec_for(dtype)) {
+    int dev = 0;
+    st = plan_async(batch, channels, inner, num_groups, dtype, &dev, &p);
+    if (st != -1) {
+      if (st != KAT_OK) return st;
+      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
+          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+        return KAT_ERR_WORKSPACE;
+      if (launch_bwd_async(dtype, x, grad_out, grad_x, numerator, denominator,
+                           static_cast<double*>(workspace), p, s) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      return launch_reduce(workspace, denominator, grad_numerator, grad_denominator, p, peers, s);
+    }
+  }
+  if (n != 0 && vec == max_vec_for(dtype)) {
+    Pipe q;
+    int dev = 0;
+    st = plan_tma(batch, channels, inner, num_groups, dtype, true, &dev, &p, &q);
+    if (st != -1) {
+      if (st != KAT_OK) return st;
+      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
+          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+        return KAT_ERR_WORKSPACE;
+      if (allow_dynamic_smem(dev, bwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      if (launch_bwd_tma(dtype, x, grad_out, grad_x, numerator, denominator,
+                         static_cast<double*>(workspace), p, q, s) != cudaSuccess)
+        return KAT_ERR_CUDA;
+      return launch_reduce(workspace, denominator, grad_numerator, grad_denominator, p, peers, s);
+    }
+  }
+  if (n == 0) {
+    st = make_plan_impl(batch, channels, inner, num_groups, dtype, vec, 1, 1, &p);
+  } else {
+    st = plan_for_launch(bwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype,
+                         vec, &p);
+  }
+  if (st != KAT_OK) return st;
+  if (p.blocks > 0) {
+    if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
+        (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+      return KAT_ERR_WORKSPACE;
+    if (launch_bwd(dtype, vec, x, grad_out, grad_x, numerator, denominator,
+                   static_cast<double*>(workspace), p, s) != cudaSuccess)
+      return KAT_ERR_CUDA;
+  }
+  return launch_reduce(workspace, denominator, grad_numerator, grad_denominator, p, peers, s);
+}
+
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -1760,77 +2023,110 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x, const fl
                      const float* denominator, float* grad_numerator, float* grad_denominator,
                      void* workspace, size_t workspace_bytes, int64_t batch, int64_t channels,
                      int64_t inner, int64_t num_groups, int dtype, void* stream) {
-  int64_t n = 0;
-  int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
-  if (st != KAT_OK) return st;
-  if (numerator == nullptr || denominator == nullptr || grad_numerator == nullptr ||
-      grad_denominator == nullptr)
-    return KAT_ERR_NULL_POINTER;
-  if (n != 0 && (x == nullptr || grad_out == nullptr)) return KAT_ERR_NULL_POINTER;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t gw = (channels / num_groups) * inner;
-  const void* ptrs[3] = {x, grad_out, grad_x};
-  const int vec = n == 0 ? 1 : pick_vec(dtype, gw, ptrs, 3);
-  if (num_groups > 0x7fffffff) return KAT_ERR_BAD_GROUPS;
-  Plan p;
-  if (n != 0 && vec == max_vec_for(dtype)) {
-    int dev = 0;
-    st = plan_async(batch, channels, inner, num_groups, dtype, &dev, &p);
-    if (st != -1) {
-      if (st != KAT_OK) return st;
-      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
-          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
-        return KAT_ERR_WORKSPACE;
-      if (launch_bwd_async(dtype, x, grad_out, grad_x, numerator, denominator,
-                           static_cast<double*>(workspace), p, s) != cudaSuccess)
-        return KAT_ERR_CUDA;
-      kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
-          static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator,
-          p);
-      if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;
-      return KAT_OK;
+  return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype, stream,
+                  nullptr);
+}
+
+int kat_rational_enable_peer_access(int device, int peer_device) {
+  if (device == peer_device) return KAT_OK;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return KAT_ERR_CUDA;
+  if (cudaSetDevice(device) != cudaSuccess) return KAT_ERR_CUDA;
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, device, peer_device);
+  if (e == cudaSuccess && can) {
+    e = cudaDeviceEnablePeerAccess(peer_device, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+      cudaGetLastError();
+      e = cudaSuccess;
     }
+  } else if (e == cudaSuccess) {
+    e = cudaErrorPeerAccessUnsupported;
   }
-  if (n != 0 && vec == max_vec_for(dtype)) {
-    Pipe q;
-    int dev = 0;
-    st = plan_tma(batch, channels, inner, num_groups, dtype, true, &dev, &p, &q);
-    if (st != -1) {
-      if (st != KAT_OK) return st;
-      if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
-          (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
-        return KAT_ERR_WORKSPACE;
-      if (allow_dynamic_smem(dev, bwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
-        return KAT_ERR_CUDA;
-      if (launch_bwd_tma(dtype, x, grad_out, grad_x, numerator, denominator,
-                         static_cast<double*>(workspace), p, q, s) != cudaSuccess)
-        return KAT_ERR_CUDA;
-      kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
-          static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator,
-          p);
-      if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;
-      return KAT_OK;
-    }
+  cudaSetDevice(prev);
+  return e == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+// Exchange buffers (setup-time plumbing, outside the per-step path).  The local buffer is
+// allocated here so that its CUDA IPC handle covers exactly it; peers' handles are opened
+// with this process's current device current and lazy peer access, so the mapping is usable
+// by kernels on that device.
+int kat_rational_exchange_create(int64_t num_groups, void** buffer, void* ipc_handle) {
+  if (buffer == nullptr || ipc_handle == nullptr) return KAT_ERR_NULL_POINTER;
+  if (num_groups < 1) return KAT_ERR_BAD_GROUPS;
+  const size_t bytes = kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * 8;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return KAT_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return KAT_ERR_CUDA;
   }
-  if (n == 0) {
-    st = make_plan_impl(batch, channels, inner, num_groups, dtype, vec, 1, 1, &p);
-  } else {
-    st = plan_for_launch(bwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype,
-                         vec, &p);
-  }
-  if (st != KAT_OK) return st;
-  if (p.blocks > 0) {
-    if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
-        (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
-      return KAT_ERR_WORKSPACE;
-    if (launch_bwd(dtype, vec, x, grad_out, grad_x, numerator, denominator,
-                   static_cast<double*>(workspace), p, s) != cudaSuccess)
-      return KAT_ERR_CUDA;
-  }
-  kat_bwd_reduce_kernel<<<dim3(unsigned(num_groups)), dim3(kReduceThreads), 0, s>>>(
-      static_cast<const double*>(workspace), denominator, grad_numerator, grad_denominator, p);
-  if (cudaGetLastError() != cudaSuccess) return KAT_ERR_CUDA;
+  memcpy(ipc_handle, &h, sizeof(h));
+  *buffer = p;
   return KAT_OK;
+}
+
+int kat_rational_exchange_open(const void* ipc_handle, void* local_probe, void** peer_buffer) {
+  if (ipc_handle == nullptr || peer_buffer == nullptr || local_probe == nullptr)
+    return KAT_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return KAT_ERR_CUDA;
+  // Prove the mapping is reachable from this device before any kernel may touch it.
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+      cudaMemcpy(local_probe, p, 16, cudaMemcpyDeviceToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    cudaIpcCloseMemHandle(p);
+    return KAT_ERR_CUDA;
+  }
+  *peer_buffer = p;
+  return KAT_OK;
+}
+
+int kat_rational_exchange_close(void* peer_buffer) {
+  return cudaIpcCloseMemHandle(peer_buffer) == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+int kat_rational_exchange_destroy(void* buffer) {
+  return cudaFree(buffer) == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+size_t kat_rational_exchange_buffer_bytes(int64_t num_groups) {
+  if (num_groups < 1) return 0;
+  return kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * sizeof(double);
+}
+
+int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x,
+                               const float* numerator, const float* denominator,
+                               float* grad_numerator, float* grad_denominator, void* workspace,
+                               size_t workspace_bytes, int64_t batch, int64_t channels,
+                               int64_t inner, int64_t num_groups, int dtype,
+                               const kat_rational_peers* peers, void* stream) {
+  if (peers == nullptr) return KAT_ERR_NULL_POINTER;
+  if (peers->world_size < 1 || peers->world_size > KAT_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world_size || peers->timeout_ms < 1)
+    return KAT_ERR_BAD_SHAPE;
+  if (num_groups < 1 || num_groups * kAcc * int64_t(sizeof(double)) > 200 * 1024)
+    return KAT_ERR_BAD_GROUPS;
+  Peers pe;
+  memset(&pe, 0, sizeof(pe));
+  pe.world = peers->world_size;
+  pe.rank = peers->rank;
+  pe.average = peers->average ? 1 : 0;
+  pe.timeout_ms = peers->timeout_ms;
+  for (int r = 0; r < pe.world; ++r) {
+    if (peers->buffers[r] == nullptr || (reinterpret_cast<uintptr_t>(peers->buffers[r]) % 16) != 0)
+      return KAT_ERR_NULL_POINTER;
+    pe.buf[r] = static_cast<char*>(peers->buffers[r]);
+  }
+  return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype, stream,
+                  &pe);
 }
 
 }  // extern "C"

@@ -6,17 +6,27 @@ weight_denominator [G, 4] of every KAT module, 10 G floats each) are sums over t
 so ranks exchange them once per step.  The reference has no distributed layer; this is
 the B200 data-parallel design: one process per GPU, torch.distributed over NCCL.
 
-`allreduce_coefficient_grads` all-gathers every rank's flattened coefficient gradients
-and adds them in rank order in float64 on every rank, so all ranks end with bit-identical
-gradients that do not depend on the collective's internal reduction order.
+Two ways to do it:
+  * `PeerExchange` + `KAT_Group.enable_data_parallel()`: the exchange is fused into the
+    backward's gradient-reduction kernel (kat_rational_bwd_allreduce): each rank stores its
+    fp64 group sums straight into every peer's exchange buffer over NVLink, raises a flag,
+    waits (bounded) for the others and adds the ranks in rank order — one kernel, no NCCL
+    call on the step.  One node, up to 8 ranks, buffers shared through CUDA IPC.
+  * `allreduce_coefficient_grads`: after a plain backward, all-gather every rank's
+    flattened coefficient gradients (NCCL or gloo) and add them in rank order in float64.
+Both leave bit-identical gradients on every rank, independent of any library's internal
+reduction order.
 """
 
 from __future__ import annotations
 
-from typing import Iterable, List
+import ctypes
+from typing import Iterable, List, Optional
 
 import torch
 import torch.distributed as dist
+
+from . import _native
 
 
 def coefficient_parameters(module: torch.nn.Module) -> List[torch.nn.Parameter]:
@@ -96,3 +106,80 @@ def shard_rows(total_rows: int, rank: int, world: int) -> slice:
 def barrier_all(groups: Iterable = (None,)) -> None:
     for g in groups:
         dist.barrier(group=g)
+
+
+class PeerExchange:
+    """Exchange buffers of one KAT module across the ranks of a single node.
+
+    Each rank creates a zeroed buffer of kat_rational_exchange_buffer_bytes(G) bytes on its
+    GPU (kat_rational_exchange_create) and publishes its 64-byte CUDA IPC handle
+    (all_gather_object); every rank maps the others' buffers on its own device with lazy
+    peer access and checks each mapping with a small copy before any kernel uses it
+    (kat_rational_exchange_open).  `peers` is the kat_rational_peers descriptor the
+    data-parallel backward takes.  Construction is collective; close() (also run at garbage
+    collection) unmaps and frees.
+    """
+
+    def __init__(self, num_groups: int, group=None, average: bool = True,
+                 timeout_ms: int = 5000, device: Optional[torch.device] = None):
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if world > _native.KAT_MAX_PEERS:
+            raise ValueError(f"PeerExchange supports up to {_native.KAT_MAX_PEERS} ranks on one "
+                             f"node, got {world}")
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        lib = _native.lib()
+        self._lib = lib
+        self._opened: List[int] = []
+        self._local = None
+        with torch.cuda.device(device):
+            local = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            _native.check("kat_rational_exchange_create",
+                          lib.kat_rational_exchange_create(num_groups, ctypes.byref(local),
+                                                           handle))
+            self._local = local.value
+            handles: list = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            probe = torch.empty(16, dtype=torch.uint8, device=device)
+            ptrs = []
+            for r in range(world):
+                if r == rank:
+                    ptrs.append(self._local)
+                    continue
+                peer = ctypes.c_void_p()
+                h = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+                _native.check("kat_rational_exchange_open",
+                              lib.kat_rational_exchange_open(h, ctypes.c_void_p(probe.data_ptr()),
+                                                             ctypes.byref(peer)))
+                self._opened.append(peer.value)
+                ptrs.append(peer.value)
+        self.peers = _native.KatPeers()
+        self.peers.world_size = world
+        self.peers.rank = rank
+        self.peers.average = 1 if average else 0
+        self.peers.timeout_ms = int(timeout_ms)
+        for r, ptr in enumerate(ptrs):
+            self.peers.buffers[r] = ctypes.c_void_p(ptr)
+        self.group = group
+        self.device = device
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free the local one (after all kernels using them)."""
+        if self._lib is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for ptr in self._opened:
+            self._lib.kat_rational_exchange_close(ctypes.c_void_p(ptr))
+        self._opened = []
+        if self._local is not None:
+            self._lib.kat_rational_exchange_destroy(ctypes.c_void_p(self._local))
+            self._local = None
+        self._lib = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

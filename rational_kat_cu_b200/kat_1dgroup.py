@@ -19,7 +19,7 @@ import torch.nn as nn
 
 from ._init_table import INIT_JSON
 from .kat_1dgroup_torch import Rational_CUDA_A_1DGroup
-from .rational_cuda import RationalCUDA1DGroup
+from .rational_cuda import RationalCUDA1DGroupDP, RationalCUDA1DGroup
 
 
 class KAT_Group(nn.Module):
@@ -65,10 +65,25 @@ class KAT_Group(nn.Module):
         assert input.dim() == 3 or input.dim() == 2, \
             "Input tensor must be 3D (batch, length, channels) or 2D (batch, channels)."
         weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
+        if getattr(self, "exchange", None) is not None:
+            return RationalCUDA1DGroupDP.apply(input, weight_numerator, self.weight_denominator,
+                                               self.num_groups, self.exchange)
         if self.rational is Rational_CUDA_A_1DGroup and input.dim() == 2:
             return self.rational(input.unsqueeze(0), weight_numerator, self.weight_denominator,
                                  self.num_groups).squeeze(0)
         return self.rational(input, weight_numerator, self.weight_denominator, self.num_groups)
+
+    def enable_data_parallel(self, group=None, average: bool = True,
+                             timeout_ms: int = 5000) -> None:
+        """Exchange this module's coefficient gradients with the other ranks of `group`
+        inside the backward's reduction kernel (NVLink peer memory, one node, up to 8 ranks):
+        every rank then holds the same rank-order sum (average by default).  Collective: call
+        it on every rank, in the same module order."""
+        from .distributed import PeerExchange
+
+        self.exchange = PeerExchange(self.num_groups, group=group, average=average,
+                                     timeout_ms=timeout_ms,
+                                     device=self.weight_denominator.device)
 
     def extra_repr(self) -> str:
         return f"num_groups={self.num_groups}, order={self.order}"

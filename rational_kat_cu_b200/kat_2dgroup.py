@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from ._init_table import INIT_JSON
-from .rational_cuda import RationalCUDA2D
+from .rational_cuda import RationalCUDA2DDP, RationalCUDA2D
 
 
 class KAT_Group2D(nn.Module):
@@ -51,7 +51,22 @@ class KAT_Group2D(nn.Module):
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         assert input.dim() == 4, "Input tensor must be 4D (batch, channels, height, width)."
         weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
+        if getattr(self, "exchange", None) is not None:
+            return RationalCUDA2DDP.apply(input, weight_numerator, self.weight_denominator,
+                                          self.num_groups, self.exchange)
         return self.rational(input, weight_numerator, self.weight_denominator, self.num_groups)
+
+    def enable_data_parallel(self, group=None, average: bool = True,
+                             timeout_ms: int = 5000) -> None:
+        """Exchange this module's coefficient gradients with the other ranks of `group`
+        inside the backward's reduction kernel (NVLink peer memory, one node, up to 8 ranks):
+        every rank then holds the same rank-order sum (average by default).  Collective: call
+        it on every rank, in the same module order."""
+        from .distributed import PeerExchange
+
+        self.exchange = PeerExchange(self.num_groups, group=group, average=average,
+                                     timeout_ms=timeout_ms,
+                                     device=self.weight_denominator.device)
 
     def extra_repr(self) -> str:
         return f"num_groups={self.num_groups}, order={self.order}"

@@ -111,7 +111,7 @@ def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims) -> Tensor:
 
 
 def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
-         need_dx: bool = True):
+         need_dx: bool = True, exchange=None):
     _check_counts(n, d, group)
     _check_cuda("input", x)
     _check_cuda("grad_output", grad_output)
@@ -130,11 +130,15 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
     with torch.cuda.device(x.device):
         ws_bytes = _workspace_bytes(dims, group, code, x.device)
         ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
-        status = _native.lib().kat_rational_bwd(
-            x.data_ptr(), grad_output.data_ptr(), d_x.data_ptr() if d_x is not None else None,
-            n32.data_ptr(), d32.data_ptr(), d_n.data_ptr(), d_d.data_ptr(),
-            ws.data_ptr(), ws.numel(), dims[0], dims[1], dims[2], group, code,
-            _stream_ptr(x.device))
+        args = (x.data_ptr(), grad_output.data_ptr(),
+                d_x.data_ptr() if d_x is not None else None, n32.data_ptr(), d32.data_ptr(),
+                d_n.data_ptr(), d_d.data_ptr(), ws.data_ptr(), ws.numel(), dims[0], dims[1],
+                dims[2], group, code)
+        if exchange is None:
+            status = _native.lib().kat_rational_bwd(*args, _stream_ptr(x.device))
+        else:
+            status = _native.lib().kat_rational_bwd_allreduce(
+                *args, ctypes.byref(exchange.peers), _stream_ptr(x.device))
     _native.check("kat_rational_bwd", status)
     return d_x, d_n, d_d
 
@@ -213,6 +217,49 @@ class RationalCUDA2D(torch.autograd.Function):
                                      group, _dims_2d(input, group),
                                      need_dx=ctx.needs_input_grad[0])
         return d_input, d_num, d_den, None
+
+
+class RationalCUDA1DGroupDP(torch.autograd.Function):
+    """RationalCUDA1DGroup whose backward also exchanges the coefficient gradients with the
+    other ranks of `exchange` (a distributed.PeerExchange) inside the reduction kernel."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
+    def forward(ctx, input, weight_numerator, weight_denominator, group, exchange):
+        ctx.save_for_backward(input, weight_numerator, weight_denominator)
+        ctx.group = group
+        ctx.exchange = exchange
+        return rational_fwd_cuda(input, weight_numerator, weight_denominator, group)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output):
+        input, weight_numerator, weight_denominator = ctx.saved_tensors
+        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
+                                     ctx.group, _dims_1d(input, ctx.group),
+                                     need_dx=ctx.needs_input_grad[0], exchange=ctx.exchange)
+        return d_input, d_num, d_den, None, None
+
+
+class RationalCUDA2DDP(torch.autograd.Function):
+    """RationalCUDA2D with the cross-rank coefficient-gradient exchange in its backward."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
+    def forward(ctx, input, weight_numerator, weight_denominator, group, exchange):
+        ctx.save_for_backward(input, weight_numerator, weight_denominator)
+        ctx.group = group
+        ctx.exchange = exchange
+        return rational_fwd_cuda_2d(input, weight_numerator, weight_denominator, group)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output):
+        input, weight_numerator, weight_denominator = ctx.saved_tensors
+        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
+                                     ctx.group, _dims_2d(input, ctx.group),
+                                     need_dx=ctx.needs_input_grad[0], exchange=ctx.exchange)
+        return d_input, d_num, d_den, None, None
 
 
 # The reference's export names (kat_rational/__init__.py:2, rational_triton2d.py:226).

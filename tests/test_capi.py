@@ -80,7 +80,9 @@ def test_argument_errors_return_before_any_launch():
 # ---------------------------------------------------------------------------
 
 def block_items(p, blk):
-    return p["items"] * blk // p["blocks"], p["items"] * (blk + 1) // p["blocks"]
+    q, r = divmod(p["items"], p["blocks"])
+    i0 = blk * q + min(blk, r)
+    return i0, i0 + q + (1 if blk < r else 0)
 
 
 def simulate(p):
@@ -187,3 +189,28 @@ def test_headline_plan_is_balanced():
     assert p["col_blocks"] == 1 and p["tile_cols"] == 384 and p["blocks"] == 148
     sizes = {block_items(p, b)[1] - block_items(p, b)[0] for b in range(p["blocks"])}
     assert max(sizes) - min(sizes) <= 1
+
+
+def _divider(d):
+    """The multiply-shift constants the library derives for an invariant divisor d
+    (Granlund-Montgomery round-up method, N = 64)."""
+    l = 0
+    while l < 64 and (1 << l) < d:
+        l += 1
+    m = ((1 << 64) * ((1 << l) - d)) // d + 1
+    return m, min(l, 1), max(l - 1, 0)
+
+
+@pytest.mark.parametrize("d", [1, 2, 3, 7, 48, 197, 25088, 25216, 100352, (1 << 31) - 1,
+                               (1 << 40) + 3, (1 << 63)])
+def test_invariant_division_formula(d):
+    import random
+
+    m, s1, s2 = _divider(d)
+    rng = random.Random(d)
+    ns = [0, 1, d - 1, d, d + 1, 2 * d - 1, (1 << 63) - 1, (1 << 64) - 1]
+    ns += [rng.randrange(0, 1 << 64) for _ in range(200)] + [rng.randrange(0, 1 << 40) for _ in range(200)]
+    for n in ns:
+        t = (m * n) >> 64
+        q = (t + ((n - t) >> s1)) >> s2
+        assert q == n // d, (n, d)
