@@ -383,6 +383,7 @@ __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[k
   q = fma_(q, x, c.c1);
   dq = fma_(dq, x, q);
   q = fma_(q, x, c.one);
+  const L x2 = mul_(x, x);
   L r = rcp_(q);
   if constexpr (kRefine) {  // Newton-Raphson: r <- r + r (1 - q r)
     const L e = fma_(neg_(q), r, c.one);
@@ -392,7 +393,6 @@ __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[k
   const L y = mul_(p, r);             // P / Q
   const L t = fma_(neg_(y), dq, dp);  // P' - y Q'
   const L w = mul_(u, y);             // go P / Q^2
-  const L x2 = mul_(x, x);
   const L x3 = mul_(x2, x);
   const L x4 = mul_(x2, x2);
   const L x5 = mul_(x4, x);
@@ -1294,7 +1294,8 @@ int validate_dims(int64_t batch, int64_t channels, int64_t inner, int64_t num_gr
 int max_vec_for(int dtype) { return 16 / elem_bytes(dtype); }
 
 int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-                   int vec, int sm_count, int ctas_per_sm, Plan* p, int max_cols = kMaxThreads) {
+                   int vec, int sm_count, int ctas_per_sm, Plan* p, int max_cols = kMaxThreads,
+                   int max_threads = kMaxThreads) {
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
@@ -1322,17 +1323,18 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   }
   if (p->vec_cols <= max_cols) {
     p->tile_cols = int32_t(p->vec_cols);
-    int64_t tr = max_cols / p->tile_cols;
-    if (tr > batch) tr = batch;
-    if (tr < 1) tr = 1;
-    p->tile_rows = int32_t(tr);
   } else {
     const int64_t ncb = (p->vec_cols + max_cols - 1) / max_cols;
     int64_t tcols = (p->vec_cols + ncb - 1) / ncb;
     tcols = (tcols + 31) / 32 * 32;
     if (tcols > max_cols) tcols = max_cols;
     p->tile_cols = int32_t(tcols);
-    p->tile_rows = 1;
+  }
+  {
+    int64_t tr = max_threads / p->tile_cols;
+    if (tr > batch) tr = batch;
+    if (tr < 1) tr = 1;
+    p->tile_rows = int32_t(tr);
   }
   const int64_t used = int64_t(p->tile_cols) * p->tile_rows;
   p->threads = int32_t((used + 31) / 32 * 32);
@@ -1706,6 +1708,10 @@ cudaError_t launch_bwd_tma_t(const void* x, const void* gy, void* dx, const floa
 #ifndef KAT_ASYNC_ROWS
 #define KAT_ASYNC_ROWS 2
 #endif
+#ifndef KAT_ASYNC_COLS
+#define KAT_ASYNC_COLS 128
+#endif
+constexpr int kAsyncCols = KAT_ASYNC_COLS;
 constexpr int kAsyncStages = KAT_ASYNC_STAGES;
 constexpr int kAsyncRows = KAT_ASYNC_ROWS;
 
@@ -1732,11 +1738,13 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
   int sms = 0;
   if (device_sm_count(dev, &sms) != cudaSuccess) return KAT_ERR_CUDA;
-  static const int max_cols = std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kMaxThreads),
-                                        kMaxThreads) / 32 * 32;
+  // Block shape of the cp.async backward: at most kAsyncCols vector columns, and as many
+  // rows as fill kMaxThreads threads (at 128 registers, one 512-thread block per SM).
+  static const int max_cols =
+      std::max(32, std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kAsyncCols), kMaxThreads) / 32 * 32);
   Plan probe;
   int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
-                          std::max(32, max_cols));
+                          max_cols);
   if (st != KAT_OK) return st;
   const void* fn = bwd_async_kernel_for(dtype);
   const size_t smem = async_smem_bytes(probe.threads);
@@ -1757,8 +1765,7 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
       g_occupancy[key] = occ;
     }
   }
-  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p,
-                      std::max(32, max_cols));
+  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p, max_cols);
   *dev_out = dev;
   return st;
 }
