@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="CPU budget of the reference-path baseline")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="print one line per bandwidth-sweep point (kernel timings) instead")
     return ap.parse_args()
 
 
@@ -215,7 +217,7 @@ def run_reference(args):
         return
     from rational_kat_cu_b200 import workloads
 
-    w = workloads.BY_NAME[args.workload]()
+    w = workloads.get(args.workload)
     rate, info = cpu_reference_rate(w, budget_s=min(150.0, 10.0 + 0.5 * (args.steps + args.warmup)),
                                     steps=args.steps, warmup=args.warmup)
     line = {
@@ -254,7 +256,7 @@ def run_ours(args):
     dist = init_process_group(world, rank, local) if world > 1 else None
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    w = workloads.BY_NAME[args.workload]()
+    w = workloads.get(args.workload)
     w.x_seed += 1000 * rank
     w.gy_seed += 1000 * rank
     elem_bytes = {"f32": 4, "bf16": 2, "f16": 2}[w.dtype]
@@ -398,7 +400,8 @@ def run_ours(args):
     def e2e_step():
         mod.zero_grad(set_to_none=True)
         if dist is not None:
-            pipe.run(h_x, h_gy, h_y, h_dx)
+            pipe.run(h_x, h_gy, h_y, h_dx, wait=False)
+            pipe.wait_compute()
             kdist.allreduce_coefficient_grads(mod)
             h_grads[0].copy_(mod.weight_numerator.grad, non_blocking=True)
             h_grads[1].copy_(mod.weight_denominator.grad, non_blocking=True)
@@ -488,10 +491,94 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_sweep(args):
+    """Bandwidth sweep on one GPU: per point, C-ABI forward and backward launches on
+    device-resident inputs, `iters` of each captured in a CUDA graph and timed with CUDA events
+    around one replay; one JSON line per point."""
+    import ctypes
+
+    from rational_kat_cu_b200 import _native, workloads
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    lib = _native.lib()
+    peak, peak_kind = measured_peak()
+    stream = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    for c, g, n, dt in workloads.sweep_points():
+        w = workloads.sweep(c, g, n, dt)
+        N = w.numel
+        eb = {"f32": 4, "bf16": 2, "f16": 2}[dt]
+        code = {"f32": 0, "f16": 1, "bf16": 2}[dt]
+        x, gy = w.inputs(dev)
+        wn, wd = w.coefficients()
+        num = wn.repeat(g, 1).to(dev).contiguous()
+        den = wd.to(dev).contiguous()
+        y = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        dn = torch.empty(g, 6, device=dev)
+        dd = torch.empty(g, 4, device=dev)
+        dims = w.dims()
+        need = ctypes.c_size_t(0)
+        _native.check("ws", lib.kat_rational_bwd_workspace_size(dims[0], dims[1], dims[2], g,
+                                                                code, dev.index,
+                                                                ctypes.byref(need)))
+        ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=dev)
+        fa = (x.data_ptr(), y.data_ptr(), num.data_ptr(), den.data_ptr(), *dims, g, code, sp)
+        ba = (x.data_ptr(), gy.data_ptr(), dx.data_ptr(), num.data_ptr(), den.data_ptr(),
+              dn.data_ptr(), dd.data_ptr(), ws.data_ptr(), ws.numel(), *dims, g, code, sp)
+        iters = max(3, min(200, int(2e10 / (N * eb * 5))))
+
+        def timed(fn, a):
+            # `iters` launches captured in a CUDA graph and replayed: device time per launch
+            # without the host's per-call cost.
+            for _ in range(2):
+                _native.check("launch", fn(*a))
+            torch.cuda.synchronize(dev)
+            cap = torch.cuda.Stream(dev)
+            graph = torch.cuda.CUDAGraph()
+            ca = a[:-1] + (ctypes.c_void_p(cap.cuda_stream),)
+            cap.wait_stream(stream)
+            with torch.cuda.stream(cap):
+                graph.capture_begin()
+                for _ in range(iters):
+                    fn(*ca)
+                graph.capture_end()
+            torch.cuda.synchronize(dev)
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            del graph
+            return e0.elapsed_time(e1) / iters
+
+        f_ms = timed(lib.kat_rational_fwd, fa)
+        b_ms = timed(lib.kat_rational_bwd, ba)
+        line = {
+            "metric": "KAT_Group sweep", "workload": w.name, "channels": c, "num_groups": g,
+            "elements": N, "dtype": dt, "iters": iters,
+            "fwd_ms": f_ms, "bwd_ms": b_ms,
+            "fwd_gelem_s": N / f_ms / 1e6, "fwd_bwd_gelem_s": N / (f_ms + b_ms) / 1e6,
+            "fwd_hbm_frac": 2 * N * eb / f_ms / 1e6 / peak,
+            "bwd_hbm_frac": 3 * N * eb / b_ms / 1e6 / peak,
+            "fwd_bwd_hbm_frac": 5 * N * eb / (f_ms + b_ms) / 1e6 / peak,
+            "peak_gbs": peak, "peak_source": peak_kind,
+            "l2": "larger than L2" if N * eb > L2_BYTES else "fits in L2 (inputs reused across launches)",
+        }
+        print(json.dumps(line), flush=True)
+        del x, gy, y, dx, ws
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep:
+        run_sweep(args)
     else:
         run_ours(args)
 

@@ -445,12 +445,13 @@ __device__ __forceinline__ void block_items(const Plan& p, int64_t blk, int64_t&
   i1 = i0 + p.items_q + (blk < p.items_r ? 1 : 0);
 }
 
-// Per-block, per-group reduction of one segment's per-thread sums (fixed order):
-// thread t of the `nthreads` participants stores its 10 sums, then warp w reduces
-// outputs w, w + nwarps, ... (output = local group x coefficient slot) in fp64 with a
-// fixed lane assignment and xor tree, and writes them to the block's workspace slots.
-// kNamed selects a named barrier over the participants (warp-specialised kernels)
-// instead of __syncthreads.
+// Per-block, per-group reduction of one segment's per-thread sums (fixed order): thread t
+// of the `nthreads` participants stores its 10 sums (slot-major, rows padded by one float so
+// the slots fall in different banks), then each output (local group x slot) is added in
+// fp64 over the tile's rows and its group's columns — by a warp with a fixed lane split and
+// xor tree when a group spans more than 32 values, else by one thread in order — and written
+// to the block's workspace slot.  kNamed selects a named barrier over the participants (warp-specialised
+// kernels) instead of __syncthreads.
 template <bool kNamed>
 __device__ __forceinline__ void participants_sync(int nthreads) {
   if constexpr (kNamed) {
@@ -468,31 +469,50 @@ __device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float*
 #pragma unroll
   for (int k = 0; k < kAcc; ++k) s_acc[k * stride + tid] = sums[k];
   participants_sync<kNamed>(nthreads);
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int nwarps = nthreads >> 5;
   const int64_t col0 = cb * p.tile_cols;
   const int64_t col_end = min(col0 + p.tile_cols, p.vec_cols);
   const int64_t g_first = col0 / p.vec_group;
   const int64_t g_last = (col_end - 1) / p.vec_group;
   const int n_out = int(g_last - g_first + 1) * kAcc;
-  for (int o = warp; o < n_out; o += nwarps) {
-    const int lg = o / kAcc;
-    const int k = o - lg * kAcc;
-    const int64_t g = g_first + lg;
-    const int tlo = int(max(g * p.vec_group, col0) - col0);
-    const int thi = int(min((g + 1) * p.vec_group, col_end) - col0);
-    const int wcols = thi - tlo;
-    const int n = wcols * p.tile_rows;
-    double v = 0.0;
-    for (int j = lane; j < n; j += 32) {
-      const int jr = j / wcols;
-      const int jc = tlo + (j - jr * wcols);
-      v += double(s_acc[k * stride + jr * p.tile_cols + jc]);
-    }
+  const int64_t span = min(int64_t(p.tile_cols), p.vec_group) * p.tile_rows;
+  if (span > 32) {
+    // Wide groups: warp w adds outputs w, w + nwarps, ...; lane j takes columns j, j+32, ...
+    // of every row, then a fixed xor tree.
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int nwarps = nthreads >> 5;
+    for (int o = warp; o < n_out; o += nwarps) {
+      const int lg = o / kAcc;
+      const int k = o - lg * kAcc;
+      const int64_t g = g_first + lg;
+      const int tlo = int(max(g * p.vec_group, col0) - col0);
+      const int thi = int(min((g + 1) * p.vec_group, col_end) - col0);
+      double v = 0.0;
+      const float* base = s_acc + k * stride;
+      for (int r = 0; r < p.tile_rows; ++r) {
+        const float* row = base + r * p.tile_cols;
+        for (int c = tlo + lane; c < thi; c += 32) v += double(row[c]);
+      }
 #pragma unroll
-    for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-    if (lane == 0) partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+      for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+      if (lane == 0) partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+    }
+  } else {
+    // Narrow groups: thread o adds output o = (local group, slot) over its rows and columns.
+    for (int o = tid; o < n_out; o += nthreads) {
+      const int lg = o / kAcc;
+      const int k = o - lg * kAcc;
+      const int64_t g = g_first + lg;
+      const int tlo = int(max(g * p.vec_group, col0) - col0);
+      const int thi = int(min((g + 1) * p.vec_group, col_end) - col0);
+      double v = 0.0;
+      const float* base = s_acc + k * stride;
+      for (int r = 0; r < p.tile_rows; ++r) {
+        const float* row = base + r * p.tile_cols;
+        for (int c = tlo; c < thi; ++c) v += double(row[c]);
+      }
+      partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+    }
   }
   participants_sync<kNamed>(nthreads);
 }
@@ -565,7 +585,7 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
   using L = typename std::conditional<V == 1, float, float2>::type;
   using Raw = typename RawOf<Tio, V>::T;
   constexpr bool kRefine = sizeof(Tio) == 4;
-  __shared__ float s_acc[kAcc][kMaxThreads];
+  __shared__ float s_acc[kAcc][kMaxThreads + 1];
 
   const int tc = threadIdx.x % p.tile_cols;
   const int tr = threadIdx.x / p.tile_cols;
@@ -637,7 +657,7 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
     float sums[kAcc];
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) sums[k] = lane_sum(acc[k]);
-    segment_reduce<false>(sums, &s_acc[0][0], kMaxThreads, threadIdx.x, blockDim.x, p, cb,
+    segment_reduce<false>(sums, &s_acc[0][0], kMaxThreads + 1, threadIdx.x, blockDim.x, p, cb,
                           cb - cb0, blockIdx.x, partial);
     i = seg_end;
   }
@@ -763,7 +783,7 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
     float sums[kAcc];
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) sums[k] = lane_sum(acc[k]);
-    segment_reduce<false>(sums, s_acc, T, tid, T, p, cb, cb - cb0, blockIdx.x, partial);
+    segment_reduce<false>(sums, s_acc, T + 1, tid, T, p, cb, cb - cb0, blockIdx.x, partial);
     i = seg_end;
   }
 }
@@ -1139,8 +1159,8 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
         sums[a] = lane_sum(acc[a]);
         acc[a] = make_float2(0.0f, 0.0f);
       }
-      segment_reduce<true>(sums, s_acc, nthreads, ctid, nthreads, p, cb, cb - cb0, blockIdx.x,
-                           partial);
+      segment_reduce<true>(sums, s_acc, nthreads + 1, ctid, nthreads, p, cb, cb - cb0,
+                           blockIdx.x, partial);
     }
   }
 }
@@ -1479,8 +1499,62 @@ int pick_vec(int dtype, int64_t group_width, const void* const* ptrs, int n_ptrs
   }
 }
 
+// Plans are pure functions of (device, kernel family, shape, dtype, vector width) once the
+// device's SM count and the kernel's occupancy are known; cache them so repeated calls on
+// the same shape skip the planning arithmetic and the cache lookups it makes.
+struct PlanKey {
+  int dev;
+  const void* fn;   // the kernel the plan is for
+  int dtype, vec;
+  int64_t batch, channels, inner, groups;
+  bool operator<(const PlanKey& o) const {
+    return std::tie(dev, fn, dtype, vec, batch, channels, inner, groups) <
+           std::tie(o.dev, o.fn, o.dtype, o.vec, o.batch, o.channels, o.inner, o.groups);
+  }
+};
+struct PlanEntry {
+  int status;
+  Plan plan;
+  Pipe pipe;
+};
+std::mutex g_plan_mu;
+std::map<PlanKey, PlanEntry> g_plan_cache;
+constexpr size_t kPlanCacheMax = 4096;
+
+bool plan_cache_get(const PlanKey& k, PlanEntry* e) {
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  auto it = g_plan_cache.find(k);
+  if (it == g_plan_cache.end()) return false;
+  *e = it->second;
+  return true;
+}
+void plan_cache_put(const PlanKey& k, const PlanEntry& e) {
+  std::lock_guard<std::mutex> lock(g_plan_mu);
+  if (g_plan_cache.size() >= kPlanCacheMax) g_plan_cache.clear();
+  g_plan_cache[k] = e;
+}
+
+int plan_for_launch_uncached(const void* fn, int64_t batch, int64_t channels, int64_t inner,
+                             int64_t num_groups, int dtype, int vec, Plan* p);
+
 int plan_for_launch(const void* fn, int64_t batch, int64_t channels, int64_t inner,
                     int64_t num_groups, int dtype, int vec, Plan* p) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  const PlanKey key{dev, fn, dtype, vec, batch, channels, inner, num_groups};
+  PlanEntry e;
+  if (plan_cache_get(key, &e)) {
+    *p = e.plan;
+    return e.status;
+  }
+  e.status = plan_for_launch_uncached(fn, batch, channels, inner, num_groups, dtype, vec, &e.plan);
+  if (e.status == KAT_OK) plan_cache_put(key, e);
+  *p = e.plan;
+  return e.status;
+}
+
+int plan_for_launch_uncached(const void* fn, int64_t batch, int64_t channels, int64_t inner,
+                             int64_t num_groups, int dtype, int vec, Plan* p) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
   int sms = 0;
@@ -1613,7 +1687,7 @@ bool make_pipe(const Plan& p, int tensors, bool bwd, Pipe* q) {
   int64_t rows = stage_target_bytes() / group_bytes;
   if (rows < 1) rows = 1;
   q->stage_rows = int32_t(rows * p.tile_rows);
-  const int64_t acc_bytes = bwd ? int64_t(kAcc) * p.threads * 4 : 0;
+  const int64_t acc_bytes = bwd ? int64_t(kAcc) * (p.threads + 1) * 4 : 0;
   const int64_t budget = kPipeSmemBudget / tma_ctas_per_sm() - kPipeHeader - acc_bytes;
   int64_t stage_bytes = int64_t(q->stage_rows) * q->seg_bytes * tensors;
   int64_t stages = budget / stage_bytes;
@@ -1665,8 +1739,30 @@ const void* bwd_tma_kernel_for(int dtype) {
 
 // Plan + slot geometry of the pipelined kernels (one block per SM).  Returns KAT_OK,
 // an error, or -1 when the pipelined kernels do not apply to this shape.
+int plan_tma_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
+                      int dtype, bool bwd, int* dev_out, Plan* p, Pipe* q);
+
 int plan_tma(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
              bool bwd, int* dev_out, Plan* p, Pipe* q) {
+  if (!bulk_pipeline_enabled()) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  const PlanKey key{dev, bwd ? bwd_tma_kernel_for(dtype) : fwd_tma_kernel_for(dtype), dtype,
+                    max_vec_for(dtype), batch, channels, inner, num_groups};
+  PlanEntry e;
+  if (!plan_cache_get(key, &e)) {
+    e.status = plan_tma_uncached(batch, channels, inner, num_groups, dtype, bwd, dev_out, &e.plan,
+                                 &e.pipe);
+    if (e.status == KAT_OK || e.status == -1) plan_cache_put(key, e);
+  }
+  *dev_out = dev;
+  *p = e.plan;
+  *q = e.pipe;
+  return e.status;
+}
+
+int plan_tma_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
+                      int dtype, bool bwd, int* dev_out, Plan* p, Pipe* q) {
   const int vmax = max_vec_for(dtype);
   const int64_t gw = (channels / num_groups) * inner;
   if (!bulk_pipeline_enabled() || gw % vmax != 0) return -1;
@@ -1716,7 +1812,7 @@ constexpr int kAsyncStages = KAT_ASYNC_STAGES;
 constexpr int kAsyncRows = KAT_ASYNC_ROWS;
 
 size_t async_smem_bytes(int threads) {
-  return size_t(kAsyncStages) * kAsyncRows * 2 * 16 * threads + size_t(kAcc) * 4 * threads;
+  return size_t(kAsyncStages) * kAsyncRows * 2 * 16 * threads + size_t(kAcc) * 4 * (threads + 1);
 }
 
 const void* bwd_async_kernel_for(int dtype) {
@@ -1729,8 +1825,28 @@ const void* bwd_async_kernel_for(int dtype) {
 
 // Plan of the cp.async backward: occupancy from the kernel's registers and its shared
 // memory at this block size.  Returns -1 when it does not apply.
+int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
+                        int dtype, int* dev_out, Plan* p);
+
 int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
                int* dev_out, Plan* p) {
+  if (pipeline_mode() != 0) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
+  const PlanKey key{dev, bwd_async_kernel_for(dtype), dtype, max_vec_for(dtype), batch, channels,
+                    inner, num_groups};
+  PlanEntry e;
+  if (!plan_cache_get(key, &e)) {
+    e.status = plan_async_uncached(batch, channels, inner, num_groups, dtype, dev_out, &e.plan);
+    if (e.status == KAT_OK || e.status == -1) plan_cache_put(key, e);
+  }
+  *dev_out = dev;
+  *p = e.plan;
+  return e.status;
+}
+
+int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
+                        int dtype, int* dev_out, Plan* p) {
   const int vmax = max_vec_for(dtype);
   const int64_t gw = (channels / num_groups) * inner;
   if (pipeline_mode() != 0 || gw % vmax != 0) return -1;

@@ -95,6 +95,11 @@ class HostPipeline:
         cur.wait_stream(self.comp)
         cur.wait_stream(self.d2h)
 
+    def wait_compute(self) -> None:
+        """Make the current stream wait for the kernels only (the coefficient gradients are
+        final); the downloads of y and dx may still be running."""
+        torch.cuda.current_stream(self.device).wait_stream(self.comp)
+
     def run(self, x_host: torch.Tensor, grad_host: torch.Tensor, y_host: torch.Tensor,
             dx_host: torch.Tensor, grads_host: Optional[List[torch.Tensor]] = None,
             wait: bool = True) -> None:

@@ -116,3 +116,25 @@ BY_NAME = {
     "kat_group_vitb_bf16": kat_group_vitb_bf16,
     "kat_group2d_f32": kat_group2d_f32,
 }
+
+
+def get(name: str) -> Workload:
+    """A workload by name: one of BY_NAME, or "sweep:C:G:N:dtype" for a sweep point."""
+    if name.startswith("sweep:"):
+        _, c, g, n, dt = name.split(":")
+        return sweep(int(c), int(g), int(n), dt)
+    return BY_NAME[name]()
+
+
+def sweep_points():
+    """The bandwidth-sweep points bench.py --sweep measures: C in {768, 3072, 8192},
+    G in {8, 64}, N = 2^20 .. 2^31 elements, bf16 / fp32 / fp16."""
+    pts = []
+    for dt in ("bf16", "f32", "f16"):
+        for c in (768, 3072, 8192):
+            for g in (8, 64):
+                for logn in (20, 24, 28, 30):
+                    pts.append((c, g, 1 << logn, dt))
+    for dt in ("bf16", "f32"):
+        pts.append((3072, 8, 1 << 31, dt))
+    return pts
