@@ -45,6 +45,10 @@ FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 
 
+def metric_for(workload) -> str:
+    return "rat_cuda fwd+bwd Gelem/s" if workload.formula == 1 else METRIC
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -62,6 +66,14 @@ def parse_args():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true",
                     help="print one line per bandwidth-sweep point (kernel timings) instead")
+    ap.add_argument("--vit-batch", type=int, default=128,
+                    help="per-GPU batch of the GR-KAN ViT-B/16 training step (--workload "
+                         "grkan_vit_b16)")
+    ap.add_argument("--kat-exchange", choices=["ddp", "fused"], default="ddp",
+                    help="how the ViT step exchanges the KAT coefficient gradients")
+    ap.add_argument("--vit-compare", action="store_true",
+                    help="also time the ViT step with the reference's PyTorch KAT formulation "
+                         "and with plain GELU MLPs (one GPU)")
     return ap.parse_args()
 
 
@@ -185,6 +197,12 @@ def cpu_reference_rate(workload, budget_s: float, steps: int = 0, warmup: int = 
         return x, gy
 
     def one(x, gy):
+        if workload.formula == 1:
+            from oracle import rat_torch_oracle
+
+            rat_torch_oracle.rat_forward_backward(x.reshape(-1, shape[-1]), wn.reshape(6), wd,
+                                                  gy.reshape(-1, shape[-1]))
+            return
         kat_torch_oracle.forward_backward(x, wn, wd, workload.groups, gy,
                                           layout="nchw" if workload.layout == "nchw" else "blc")
 
@@ -208,7 +226,10 @@ def cpu_reference_rate(workload, budget_s: float, steps: int = 0, warmup: int = 
     return elems / dt / 1e9, {
         "cores": cores, "rows": rows, "elements": elems, "seconds_per_step": dt, "reps": reps,
         "sample": f"x[{rows},{','.join(str(s) for s in shape[1:])}] of {workload.name} "
-                  f"(fp32 upcast), fwd+bwd, mean of {reps} timed steps"}
+                  f"(fp32 upcast), fwd+bwd"
+                  + (" (rat_cuda formula, the reference's PyTorch definition)"
+                     if workload.formula == 1 else "")
+                  + f", mean of {reps} timed steps"}
 
 
 def run_reference(args):
@@ -221,7 +242,8 @@ def run_reference(args):
     rate, info = cpu_reference_rate(w, budget_s=min(150.0, 10.0 + 0.5 * (args.steps + args.warmup)),
                                     steps=args.steps, warmup=args.warmup)
     line = {
-        "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "metric": metric_for(w), "value": rate, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": info["seconds_per_step"] * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic", "impl": "reference",
@@ -263,15 +285,22 @@ def run_ours(args):
     N = w.numel
 
     wn, wd = w.coefficients()
-    cls = kat.KAT_Group2D if w.layout == "nchw" else kat.KAT_Group
-    mod = cls(num_groups=w.groups, mode="gelu").to(dev)
+    formula = w.formula
+    if formula == 1:
+        mod = kat.RatGroup(num_groups=w.groups).to(dev)
+    else:
+        cls = kat.KAT_Group2D if w.layout == "nchw" else kat.KAT_Group
+        mod = cls(num_groups=w.groups, mode="gelu").to(dev)
     with torch.no_grad():
-        mod.weight_numerator.copy_(wn)
+        mod.weight_numerator.copy_(wn.view_as(mod.weight_numerator))
         mod.weight_denominator.copy_(wd)
-    if dist is not None:
+    eager_exchange = False
+    if dist is not None and formula == 0:
         # Coefficient gradients are exchanged inside the backward's reduction kernel over
         # NVLink peer memory (no NCCL call on the step).
         mod.enable_data_parallel(timeout_ms=20000)
+    elif dist is not None:
+        eager_exchange = True   # rat_cuda: NCCL all-gather after the backward, eager steps
     x, gy = w.inputs(dev)
     x.requires_grad_(True)
     stream = torch.cuda.current_stream(dev)
@@ -279,6 +308,8 @@ def run_ours(args):
     def step_eager():
         y = mod(x)
         y.backward(gy)
+        if eager_exchange:
+            kdist.allreduce_coefficient_grads(mod)
         return y
 
     # Warm up (also fills the workspace-size cache before any capture).
@@ -293,7 +324,7 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
 
     graph = None
-    if not args.no_graph:
+    if not args.no_graph and not eager_exchange:
         mod.zero_grad(set_to_none=True)
         x.grad = None
         graph = torch.cuda.CUDAGraph()
@@ -358,10 +389,16 @@ def run_ours(args):
     ws_buf = torch.empty(max(ws_need.value, 16), dtype=torch.uint8, device=dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
     fwd_args = (xs.data_ptr(), y_buf.data_ptr(), n_rep.data_ptr(), d_rep.data_ptr(),
-                dims[0], dims[1], dims[2], w.groups, code, sp)
+                dims[0], dims[1], dims[2], w.groups, code)
     bwd_args = (xs.data_ptr(), gy.data_ptr(), dx_buf.data_ptr(), n_rep.data_ptr(),
                 d_rep.data_ptr(), dn_buf.data_ptr(), dd_buf.data_ptr(), ws_buf.data_ptr(),
-                ws_buf.numel(), dims[0], dims[1], dims[2], w.groups, code, sp)
+                ws_buf.numel(), dims[0], dims[1], dims[2], w.groups, code)
+    if formula == 0:
+        fwd_fn, bwd_fn = lib.kat_rational_fwd, lib.kat_rational_bwd
+        fwd_args, bwd_args = fwd_args + (sp,), bwd_args + (sp,)
+    else:
+        fwd_fn, bwd_fn = lib.kat_rational_fwd_formula, lib.kat_rational_bwd_formula
+        fwd_args, bwd_args = fwd_args + (formula, sp), bwd_args + (formula, sp)
 
     def time_launches(fn, args, iters):
         for _ in range(3):
@@ -375,8 +412,8 @@ def run_ours(args):
         torch.cuda.synchronize(dev)
         return a.elapsed_time(b) / iters
 
-    fwd_ms = time_launches(lib.kat_rational_fwd, fwd_args, args.kernel_iters)
-    bwd_ms = time_launches(lib.kat_rational_bwd, bwd_args, args.kernel_iters)
+    fwd_ms = time_launches(fwd_fn, fwd_args, args.kernel_iters)
+    bwd_ms = time_launches(bwd_fn, bwd_args, args.kernel_iters)
     mode = os.environ.get("KAT_RATIONAL_PIPELINE", "async")
     bwd_kernel_name = {"registers": "kat_bwd_kernel", "bulk": "kat_bwd_tma_kernel"}.get(
         mode, "kat_bwd_async_kernel") + " + kat_bwd_reduce_kernel (one C-ABI backward call)"
@@ -448,19 +485,23 @@ def run_ours(args):
         peak, peak_kind = measured_peak()
         step_bytes = 5 * N * elem_bytes
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "metric": metric_for(w), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": w.dtype, "data": "synthetic",
             "config": {
                 "workload": w.name, "shape": list(w.shape), "num_groups": w.groups,
                 "coefficients": "gelu + N(0,0.01)" if w.perturb else w.mode,
+                "formula": "abs-after-sum (rat_cuda)" if formula == 1 else "KAT (kat_1dgroup_torch)",
                 "elements_per_gpu": N, "layout": w.layout,
                 "l2": f"inputs larger than L2 ({N * elem_bytes / 1e6:.0f} MB per tensor > "
                       f"{L2_BYTES / 1e6:.0f} MB)",
                 "step": "module forward + backward" + (" in a CUDA graph" if graph else "")
                         + (" with the coefficient-gradient exchange fused into the reduction "
-                           "kernel (NVLink peer stores)" if world > 1 else ""),
+                           "kernel (NVLink peer stores)" if world > 1 and not eager_exchange
+                           else "")
+                        + (" and an NCCL all-gather of the coefficient gradients"
+                           if eager_exchange else ""),
             },
             "roofline": {
                 "bound": "hbm", "kernel": bwd_kernel_name,
@@ -573,9 +614,286 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+# ---------------------------------------------------------------------------
+# GR-KAN ViT-B/16 data-parallel training step (--workload grkan_vit_b16)
+# ---------------------------------------------------------------------------
+
+VIT_WORKLOAD = "grkan_vit_b16"
+VIT_METRIC = "GR-KAN ViT-B/16 training images/s"
+VIT_UNIT = "images/s"
+
+
+def _time_steps(step, steps, warmup, dev, stream, dist=None):
+    """Average device time of one `step` over `steps` timed calls after `warmup` untimed ones
+    (CUDA events on `stream`, barrier + synchronize on both sides, max over ranks)."""
+    for _ in range(warmup):
+        step()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ms = a.elapsed_time(b)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / steps
+
+
+def _kat_kernel_ms(dev, stream, shape, mode, groups, iters):
+    """C-ABI forward and backward launch times (ms) of one KAT_Group at `shape` (bf16,
+    `mode` coefficients), back-to-back on device-resident buffers."""
+    import ctypes
+
+    from rational_kat_cu_b200 import _native
+    from rational_kat_cu_b200._init_table import load_table
+
+    lib = _native.lib()
+    code = _native.KAT_DTYPE_BF16
+    C = shape[-1]
+    rows = 1
+    for d in shape[:-1]:
+        rows *= d
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    gy = torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+    table = load_table()[mode]
+    num = torch.tensor(table["init_w_numerator"], device=dev).view(1, 6).repeat(groups, 1)
+    den = torch.tensor(table["init_w_denominator"], device=dev).view(1, 4).repeat(groups, 1)
+    y, dx = torch.empty_like(x), torch.empty_like(x)
+    dn = torch.empty(groups, 6, device=dev)
+    dd = torch.empty(groups, 4, device=dev)
+    need = ctypes.c_size_t(0)
+    _native.check("ws", lib.kat_rational_bwd_workspace_size(rows, C, 1, groups, code, dev.index,
+                                                            ctypes.byref(need)))
+    ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    fa = (x.data_ptr(), y.data_ptr(), num.data_ptr(), den.data_ptr(), rows, C, 1, groups, code, sp)
+    ba = (x.data_ptr(), gy.data_ptr(), dx.data_ptr(), num.data_ptr(), den.data_ptr(),
+          dn.data_ptr(), dd.data_ptr(), ws.data_ptr(), ws.numel(), rows, C, 1, groups, code, sp)
+    out = []
+    for fn, a in ((lib.kat_rational_fwd, fa), (lib.kat_rational_bwd, ba)):
+        for _ in range(3):
+            _native.check("launch", fn(*a))
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn(*a)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        out.append(e0.elapsed_time(e1) / iters)
+    return out[0], out[1], x.numel()
+
+
+def _vit_cpu_rate(budget_s: float, steps: int = 0, warmup: int = 0):
+    """The reference's CPU path for the ViT step: the same GR-KAN ViT-B/16, fp32 on the host
+    cores, its KAT activations evaluated by the oracle's restatement of kat_1dgroup_torch.py,
+    on a bounded batch.  Returns (images/s, info)."""
+    from oracle import kat_torch_oracle
+    from rational_kat_cu_b200 import grkan_vit as gv
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    cfg = gv.vit_b16()
+    torch.manual_seed(0)
+    model = gv.GRKANViT(cfg, kat_device="cpu")
+    for m in model.kat_modules():
+        m.rational = kat_torch_oracle.rational_1dgroup
+    opt = gv.make_optimizer(model)
+
+    def run(batch, n):
+        images, labels = gv.synthetic_batch(batch, cfg, dtype=torch.float32, seed=0)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            gv.train_step(model, opt, images, labels)
+        return (time.perf_counter() - t0) / max(n, 1)
+
+    per_image = run(1, 1)
+    n_calls = (steps + warmup) if steps else 2
+    batch = int(max(1, min(32, budget_s / max(n_calls, 1) / per_image)))
+    run(batch, warmup if steps else 1)
+    reps = steps if steps else 1
+    dt = run(batch, reps)
+    return batch / dt, {
+        "cores": cores, "batch": batch, "seconds_per_step": dt, "reps": reps,
+        "sample": f"GR-KAN ViT-B/16 training step (AdamW) at batch {batch}, fp32 on the host "
+                  f"cores, KAT activations by the oracle's kat_1dgroup_torch restatement, mean "
+                  f"of {reps} timed steps"}
+
+
+def run_vit_reference(args):
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    rate, info = _vit_cpu_rate(budget_s=min(150.0, 20.0 + 2.0 * (args.steps + args.warmup)),
+                               steps=min(args.steps, 3), warmup=min(args.warmup, 1))
+    line = {
+        "metric": VIT_METRIC, "value": rate, "unit": VIT_UNIT, "n_gpus": args.gpus,
+        "steps": min(args.steps, 3), "warmup": min(args.warmup, 1),
+        "ms_per_step": info["seconds_per_step"] * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": VIT_WORKLOAD, "model": "GR-KAN ViT-B/16", "image": 224,
+                   "sample_batch": info["batch"]},
+        "cpu_baseline": {"value": rate, "unit": VIT_UNIT, "cores": info["cores"], "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": rate, "unit": VIT_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_vit(args):
+    """One data-parallel training step of GR-KAN ViT-B/16 (bf16 parameters and activations,
+    AdamW) per timed iteration, `--vit-batch` synthetic 224x224 images per GPU."""
+    import dataclasses
+
+    from rational_kat_cu_b200 import grkan_vit as gv
+
+    world, rank, local = dist_setup()
+    dist = init_process_group(world, rank, local) if world > 1 else None
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    cfg = gv.vit_b16()
+    B = args.vit_batch
+
+    def build(act="kat", kat_device="cuda"):
+        torch.manual_seed(0)
+        return gv.GRKANViT(dataclasses.replace(cfg, act=act), kat_device=kat_device).to(
+            dev, dtype=torch.bfloat16)
+
+    model = build()
+    net = model
+    if dist is not None:
+        net = gv.wrap_data_parallel(model, args.kat_exchange, device_ids=[local],
+                                    timeout_ms=20000, gradient_as_bucket_view=True)
+    opt = gv.make_optimizer(model)
+    h_img, h_lab = gv.synthetic_batch(B, cfg, dtype=torch.bfloat16, seed=rank, device=dev)
+    d_img, d_lab = h_img.to(dev), h_lab.to(dev)
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = _time_steps(lambda: gv.train_step(net, opt, d_img, d_lab), args.steps, args.warmup,
+                     dev, stream, dist)
+    value = world * B / (ms * 1e-3)
+
+    # End to end: every step uploads its images and labels from pinned host memory and
+    # reads the loss back into pinned host memory.
+    h_loss = torch.empty((), dtype=torch.float32, pin_memory=True)
+
+    def e2e_step():
+        img = h_img.to(dev, non_blocking=True)
+        lab = h_lab.to(dev, non_blocking=True)
+        h_loss.copy_(gv.train_step(net, opt, img, lab), non_blocking=True)
+
+    e2e_ms = _time_steps(e2e_step, args.e2e_steps, 2, dev, stream, dist)
+    loss_value = float(h_loss.item())
+    clocks = None
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary()
+
+    # KAT kernels at the model's shapes (standalone C-ABI timings): 12 x act1 [B,197,768]
+    # 'identity' + 12 x act2 [B,197,3072] 'gelu', forward + backward.
+    f1, b1, n1 = _kat_kernel_ms(dev, stream, (B, cfg.num_tokens, cfg.embed_dim), "identity",
+                                cfg.num_groups, args.kernel_iters // 4 or 1)
+    f2, b2, n2 = _kat_kernel_ms(dev, stream, (B, cfg.num_tokens, 4 * cfg.embed_dim), "gelu",
+                                cfg.num_groups, args.kernel_iters // 4 or 1)
+    kat_ms = cfg.depth * (f1 + b1 + f2 + b2)
+    peak, peak_kind = measured_peak()
+    bwd_gbs = 3 * n2 * 2 / (b2 * 1e-3) / 1e9
+
+    compare = None
+    if args.vit_compare and world == 1:
+        compare = {}
+        del opt
+        for name, kw in (("kat_torch_formulation", dict(kat_device="cpu")),
+                         ("gelu_mlp", dict(act="gelu"))):
+            m2 = build(**kw)
+            o2 = gv.make_optimizer(m2)
+            steps2 = max(5, min(args.steps, 30))
+            ms2 = _time_steps(lambda: gv.train_step(m2, o2, d_img, d_lab), steps2, 3, dev, stream)
+            compare[name] = {"ms_per_step": ms2, "images_s": B / (ms2 * 1e-3), "steps": steps2}
+            del m2, o2
+            torch.cuda.empty_cache()
+        compare["kat_torch_formulation"]["what"] = (
+            "KAT_Group on the reference's PyTorch formulation (power stack + bmm, "
+            "kat_1dgroup_torch.py) on the GPU, everything else identical")
+        compare["gelu_mlp"]["what"] = "plain ViT-B/16 MLP (fc1 -> GELU -> fc2), no KAT"
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        rate, info = _vit_cpu_rate(budget_s=args.cpu_seconds)
+        cpu = {"value": rate, "unit": VIT_UNIT, "cores": info["cores"], "kind": "port",
+               "sample": info["sample"]}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": VIT_METRIC, "value": value, "unit": VIT_UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": VIT_WORKLOAD,
+                "model": "GR-KAN ViT-B/16 (12 layers, d=768, MLP 3072, 12 heads, KAT_Group "
+                         "act1 'identity' / act2 'gelu', 8 groups)",
+                "global_batch": B * world, "per_gpu_batch": B, "image": [3, 224, 224],
+                "seq_len": cfg.num_tokens, "parallelism": f"dp{world}",
+                "kat_exchange": args.kat_exchange if world > 1 else None,
+                "optimizer": "AdamW (fused)", "params": "bf16",
+                "l2": "activations of one step are far larger than L2 (no flush needed)",
+                "loss_last_step": loss_value,
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "KAT act2 backward call [B,197,3072] bf16 "
+                                          "(kat_bwd_async_kernel + kat_bwd_reduce_kernel)",
+                "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
+                "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "algorithmic_bytes_per_launch": 3 * n2 * 2, "ms_per_launch": b2,
+            },
+            "kat": {
+                "act1_fwd_ms": f1, "act1_bwd_ms": b1, "act2_fwd_ms": f2, "act2_bwd_ms": b2,
+                "kat_ms_per_step": kat_ms, "kat_share_of_step": kat_ms / ms,
+                "note": "standalone C-ABI timings at the model's shapes, times 12 blocks",
+            },
+            "compare": compare,
+            "e2e": {"value": world * B / (e2e_ms * 1e-3), "unit": VIT_UNIT,
+                    "h2d_bytes_per_step": world * (h_img.numel() * 2 + h_lab.numel() * 8),
+                    "d2h_bytes_per_step": world * 4, "ms_per_step": e2e_ms,
+                    "api": "grkan_vit.train_step on pinned host images/labels (H2D per step), "
+                           "loss read back to pinned host"},
+            "gpu_launches": 3 * 2 * cfg.depth * args.steps * world,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        for m in model.kat_modules():
+            if getattr(m, "exchange", None) is not None:
+                m.exchange.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.workload == VIT_WORKLOAD:
+        if args.impl == "reference":
+            run_vit_reference(args)
+        else:
+            run_vit(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.sweep:
         run_sweep(args)

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define KAT_RATIONAL_ABI_VERSION 1
+#define KAT_RATIONAL_ABI_VERSION 2
 
 /* Data-tensor element types. */
 #define KAT_DTYPE_F32 0
@@ -60,6 +60,11 @@ extern "C" {
 #define KAT_ERR_WORKSPACE 5         /* workspace NULL or smaller than required */
 #define KAT_ERR_CUDA 6              /* CUDA runtime / launch error */
 #define KAT_ERR_SCRATCH_LIMIT 7     /* kat_rational_bwd_noalloc: problem exceeds its fixed scratch */
+#define KAT_ERR_BAD_FORMULA 8       /* formula is not one of KAT_FORMULA_* */
+
+/* Denominator formulas (the *_formula entry points). */
+#define KAT_FORMULA_KAT 0      /* Q = 1 + sum_i |b_i| x^i       (kat_rational/kat_1dgroup_torch.py) */
+#define KAT_FORMULA_ABS_SUM 1  /* Q = 1 + |sum_i b_i x^i|       (rational_kat_cu rat_cuda) */
 
 /*
  * Forward: y = P(x)/Q(x).
@@ -96,6 +101,48 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x,
                      void* workspace, size_t workspace_bytes,
                      int64_t batch, int64_t channels, int64_t inner,
                      int64_t num_groups, int dtype, void* stream);
+
+/*
+ * The same forward and backward with a selectable denominator formula.
+ * formula = KAT_FORMULA_KAT is exactly kat_rational_fwd / kat_rational_bwd.
+ * formula = KAT_FORMULA_ABS_SUM is the `rat_cuda` front end of the reference:
+ *     Q(x) = 1 + |D(x)|,  D(x) = b0 x + b1 x^2 + b2 x^3 + b3 x^4  (raw coefficients,
+ *     absolute value after the sum; D by Horner, then times x)
+ * forward as kat_rational/rational_triton.py:22-72 (rational_fwd_triton, called by
+ * rational_kat_cu/__init__.py:29), backward as rational_kat_cu/rational_bwd_triton.py:
+ *     grad_x                = (P' Q - P sgn(D) D') / Q^2 * grad_out
+ *     grad_numerator[g,k]   = sum over group g of grad_out * x^k / Q
+ *     grad_denominator[g,j] = sum over group g of -grad_out * P * sgn(D) * x^(j+1) / Q^2
+ * with sgn(D) = -1 where D < 0 and +1 elsewhere (D = 0 included), as the reference
+ * kernels' where(D < 0, -1, 1).  Same layout, workspace (kat_rational_bwd_workspace_size
+ * covers both formulas), determinism and error rules as the KAT entry points.
+ * Replaces rational_kat_cu/__init__.py:29-40 (the Triton launchers of _RationalGroupedFn).
+ */
+int kat_rational_fwd_formula(const void* x, void* y,
+                             const float* numerator, const float* denominator,
+                             int64_t batch, int64_t channels, int64_t inner,
+                             int64_t num_groups, int dtype, int formula, void* stream);
+
+int kat_rational_bwd_formula(const void* x, const void* grad_out, void* grad_x,
+                             const float* numerator, const float* denominator,
+                             float* grad_numerator, float* grad_denominator,
+                             void* workspace, size_t workspace_bytes,
+                             int64_t batch, int64_t channels, int64_t inner,
+                             int64_t num_groups, int dtype, int formula, void* stream);
+
+/*
+ * Forward in float64 for float64 tensors, either formula: x, y and the coefficients
+ * (numerator [num_groups, 6], denominator [num_groups, 4]) are all double and every
+ * operation is float64.  For gradient checking: the reference's Triton forward loads its
+ * input without a cast and so evaluates float64 inputs in float64
+ * (kat_rational/rational_triton.py:36-72).  A plain grid-stride kernel (no vector path);
+ * no float64 backward is provided (the reference's backward kernels compute in fp32, and
+ * the Python wrappers run float64 backward through the fp32 entry points).
+ */
+int kat_rational_fwd_f64(const double* x, double* y,
+                         const double* numerator, const double* denominator,
+                         int64_t batch, int64_t channels, int64_t inner,
+                         int64_t num_groups, int formula, void* stream);
 
 /*
  * Backward without any device allocation, for callers that cannot allocate where they run

@@ -2,12 +2,15 @@
 
 Public API, matching the reference package `kat_rational` (kat_rational/__init__.py:1-4):
 KAT_Group, KAT_Group2D, KAT_Group_Torch and the autograd Functions (also under their
-reference names RationalTriton1DGroup / RationalTriton2D).
+reference names RationalTriton1DGroup / RationalTriton2D); and the reference package
+`rational_kat_cu`'s front end rat_cuda (rational_kat_cu/__init__.py), the abs-after-sum
+variant of the activation on the same kernels.
 """
 
 from .kat_1dgroup import KAT_Group
 from .kat_1dgroup_torch import KAT_Group_Torch, Rational_CUDA_A_1DGroup
 from .kat_2dgroup import KAT_Group2D
+from .rat_cuda import RatGroup, rat_cuda
 from .rational_cuda import (
     RationalCUDA1DGroup,
     RationalCUDA2D,
@@ -32,4 +35,6 @@ __all__ = [
     "rational_bwd_cuda",
     "rational_fwd_cuda_2d",
     "rational_bwd_cuda_2d",
+    "rat_cuda",
+    "RatGroup",
 ]

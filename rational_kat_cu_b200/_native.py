@@ -24,11 +24,18 @@ KAT_ERR_BAD_GROUPS = 4
 KAT_ERR_WORKSPACE = 5
 KAT_ERR_CUDA = 6
 KAT_ERR_SCRATCH_LIMIT = 7
+KAT_ERR_BAD_FORMULA = 8
+
+KAT_FORMULA_KAT = 0
+KAT_FORMULA_ABS_SUM = 1
 
 # Every symbol include/kat_rational.h declares.
 EXPORTED_SYMBOLS = (
     "kat_rational_fwd",
     "kat_rational_bwd",
+    "kat_rational_fwd_formula",
+    "kat_rational_fwd_f64",
+    "kat_rational_bwd_formula",
     "kat_rational_bwd_workspace_size",
     "kat_rational_strerror",
     "kat_rational_abi_version",
@@ -60,7 +67,7 @@ class KatPeers(ctypes.Structure):
         ("buffers", ctypes.c_void_p * KAT_MAX_PEERS),
     ]
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class KatPlan(ctypes.Structure):
@@ -111,6 +118,13 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_bwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_size_t,
                                      i64, i64, i64, i64, i32, vp]
     lib.kat_rational_bwd.restype = i32
+    lib.kat_rational_fwd_formula.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, vp]
+    lib.kat_rational_fwd_formula.restype = i32
+    lib.kat_rational_bwd_formula.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_size_t,
+                                             i64, i64, i64, i64, i32, i32, vp]
+    lib.kat_rational_bwd_formula.restype = i32
+    lib.kat_rational_fwd_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
+    lib.kat_rational_fwd_f64.restype = i32
     lib.kat_rational_bwd_workspace_size.argtypes = [i64, i64, i64, i64, i32, i32,
                                                     ctypes.POINTER(ctypes.c_size_t)]
     lib.kat_rational_bwd_workspace_size.restype = i32

@@ -79,6 +79,7 @@ struct Plan {
   uint64_t rows_m;     // multiply-shift constants for dividing by rows ...
   uint64_t vg_m;       // ... and by vec_group
   int32_t rows_s1, rows_s2, vg_s1, vg_s2;
+  int32_t formula;     // KAT_FORMULA_*: how the reduction signs the denominator terms
 };
 
 // Division by an invariant divisor d >= 1 with a multiply and shifts (Granlund and
@@ -303,6 +304,28 @@ template <> __device__ __forceinline__ float2 bcast<float2>(float v) { return ma
 __device__ __forceinline__ float lane_sum(float v) { return v; }
 __device__ __forceinline__ float lane_sum(float2 v) { return v.x + v.y; }
 
+// Two elements computed with scalar fp32 instructions (the fp32 backward: measured faster
+// there than the paired instructions, while 16-bit inputs gain from pairing).
+struct S2 {
+  float x, y;
+};
+__device__ __forceinline__ S2 fma_(S2 a, S2 b, S2 c) {
+  return S2{__fmaf_rn(a.x, b.x, c.x), __fmaf_rn(a.y, b.y, c.y)};
+}
+__device__ __forceinline__ S2 mul_(S2 a, S2 b) { return S2{__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)}; }
+__device__ __forceinline__ S2 add_(S2 a, S2 b) { return S2{__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y)}; }
+__device__ __forceinline__ S2 neg_(S2 a) { return S2{-a.x, -a.y}; }
+__device__ __forceinline__ S2 rcp_(S2 q) { return S2{rcp_(q.x), rcp_(q.y)}; }
+template <> __device__ __forceinline__ S2 bcast<S2>(float v) { return S2{v, v}; }
+__device__ __forceinline__ float lane_sum(S2 v) { return v.x + v.y; }
+
+// Pair <-> lane type.
+template <typename L> __device__ __forceinline__ L to_lane(float2 v);
+template <> __device__ __forceinline__ float2 to_lane<float2>(float2 v) { return v; }
+template <> __device__ __forceinline__ S2 to_lane<S2>(float2 v) { return S2{v.x, v.y}; }
+__device__ __forceinline__ float2 from_lane(float2 v) { return v; }
+__device__ __forceinline__ float2 from_lane(S2 v) { return make_float2(v.x, v.y); }
+
 // Coefficients of one group, broadcast to the lane type.
 template <typename L> struct FwdCoef {
   L a0, a1, a2, a3, a4, a5;  // numerator
@@ -316,7 +339,19 @@ template <typename L> struct BwdCoef {
   L one;
 };
 
-template <typename L>
+// Denominator formulas.  kFormulaKat: Q = 1 + sum_i |b_i| x^i (coefficients made
+// non-negative once, kat_rational/kat_1dgroup_torch.py:63-69).  kFormulaAbsSum:
+// Q = 1 + |D(x)|, D = sum_i b_i x^i with raw coefficients and the absolute value taken after
+// the sum (rational_kat_cu/__init__.py:13-18, kat_rational/rational_triton.py:65-72).
+constexpr int kFormulaKat = KAT_FORMULA_KAT;
+constexpr int kFormulaAbsSum = KAT_FORMULA_ABS_SUM;
+
+template <int kF>
+__device__ __forceinline__ float den_coef(const float* b, int i) {
+  return kF == kFormulaKat ? fabsf(__ldg(b + i)) : __ldg(b + i);
+}
+
+template <typename L, int kF>
 __device__ __forceinline__ void load_fwd_coef(const float* __restrict__ num,
                                               const float* __restrict__ den, int64_t g,
                                               FwdCoef<L>& c) {
@@ -324,12 +359,12 @@ __device__ __forceinline__ void load_fwd_coef(const float* __restrict__ num,
   const float* b = den + g * 4;
   c.a0 = bcast<L>(__ldg(a + 0)); c.a1 = bcast<L>(__ldg(a + 1)); c.a2 = bcast<L>(__ldg(a + 2));
   c.a3 = bcast<L>(__ldg(a + 3)); c.a4 = bcast<L>(__ldg(a + 4)); c.a5 = bcast<L>(__ldg(a + 5));
-  c.c1 = bcast<L>(fabsf(__ldg(b + 0))); c.c2 = bcast<L>(fabsf(__ldg(b + 1)));
-  c.c3 = bcast<L>(fabsf(__ldg(b + 2))); c.c4 = bcast<L>(fabsf(__ldg(b + 3)));
+  c.c1 = bcast<L>(den_coef<kF>(b, 0)); c.c2 = bcast<L>(den_coef<kF>(b, 1));
+  c.c3 = bcast<L>(den_coef<kF>(b, 2)); c.c4 = bcast<L>(den_coef<kF>(b, 3));
   c.one = bcast<L>(1.0f);
 }
 
-template <typename L>
+template <typename L, int kF>
 __device__ __forceinline__ void load_bwd_coef(const float* __restrict__ num,
                                               const float* __restrict__ den, int64_t g,
                                               BwdCoef<L>& c) {
@@ -337,13 +372,26 @@ __device__ __forceinline__ void load_bwd_coef(const float* __restrict__ num,
   const float* b = den + g * 4;
   c.a0 = bcast<L>(__ldg(a + 0)); c.a1 = bcast<L>(__ldg(a + 1)); c.a2 = bcast<L>(__ldg(a + 2));
   c.a3 = bcast<L>(__ldg(a + 3)); c.a4 = bcast<L>(__ldg(a + 4)); c.a5 = bcast<L>(__ldg(a + 5));
-  c.c1 = bcast<L>(fabsf(__ldg(b + 0))); c.c2 = bcast<L>(fabsf(__ldg(b + 1)));
-  c.c3 = bcast<L>(fabsf(__ldg(b + 2))); c.c4 = bcast<L>(fabsf(__ldg(b + 3)));
+  c.c1 = bcast<L>(den_coef<kF>(b, 0)); c.c2 = bcast<L>(den_coef<kF>(b, 1));
+  c.c3 = bcast<L>(den_coef<kF>(b, 2)); c.c4 = bcast<L>(den_coef<kF>(b, 3));
   c.one = bcast<L>(1.0f);
 }
 
+// |v| and v with its sign flipped where s < 0 (s = -0 counts as non-negative, as the
+// reference's where(D < 0, -1, 1)).
+__device__ __forceinline__ float abs_(float v) { return fabsf(v); }
+__device__ __forceinline__ float2 abs_(float2 v) { return make_float2(fabsf(v.x), fabsf(v.y)); }
+__device__ __forceinline__ float flip_neg_(float v, float s) { return s < 0.0f ? -v : v; }
+__device__ __forceinline__ float2 flip_neg_(float2 v, float2 s) {
+  return make_float2(flip_neg_(v.x, s.x), flip_neg_(v.y, s.y));
+}
+__device__ __forceinline__ S2 abs_(S2 v) { return S2{fabsf(v.x), fabsf(v.y)}; }
+__device__ __forceinline__ S2 flip_neg_(S2 v, S2 s) {
+  return S2{flip_neg_(v.x, s.x), flip_neg_(v.y, s.y)};
+}
+
 // Forward on one lane (scalar or pair).
-template <typename L, bool kExactDiv>
+template <typename L, bool kExactDiv, int kF>
 __device__ __forceinline__ L fwd_math(L x, const FwdCoef<L>& c) {
   L p = fma_(c.a5, x, c.a4);
   p = fma_(p, x, c.a3);
@@ -353,7 +401,11 @@ __device__ __forceinline__ L fwd_math(L x, const FwdCoef<L>& c) {
   L q = fma_(c.c4, x, c.c3);
   q = fma_(q, x, c.c2);
   q = fma_(q, x, c.c1);
-  q = fma_(q, x, c.one);
+  if constexpr (kF == kFormulaKat) {
+    q = fma_(q, x, c.one);
+  } else {
+    q = add_(abs_(mul_(q, x)), c.one);  // 1 + |D|, D = (Horner of b3..b0) * x
+  }
   if constexpr (kExactDiv) {
     return div_rn_(p, q);
   } else {
@@ -363,7 +415,7 @@ __device__ __forceinline__ L fwd_math(L x, const FwdCoef<L>& c) {
 
 // Backward on one lane: returns dx and adds this lane's gradient terms into
 // acc[0..5] (sum u x^k) and acc[6..9] (sum u y x^i, i = 1..4).
-template <typename L, bool kRefine>
+template <typename L, bool kRefine, int kF>
 __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[kAcc]) {
   // Horner for P and Q; the derivatives come from the same partial sums
   // (d_k = d_{k+1} x + p_{k+1}), so no scaled coefficients are needed.
@@ -382,7 +434,16 @@ __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[k
   dq = fma_(dq, x, q);
   q = fma_(q, x, c.c1);
   dq = fma_(dq, x, q);
-  q = fma_(q, x, c.one);
+  L d_sign;  // abs-after-sum: D, whose sign flips Q' and the denominator gradient terms
+  if constexpr (kF == kFormulaKat) {
+    q = fma_(q, x, c.one);
+  } else {
+    // Here q = h(x) = D / x (the Horner value before its last step) and dq = D' (the
+    // derivative recurrence has run to its end): D = h x, Q = 1 + |D|, Q' = sgn(D) D'.
+    d_sign = mul_(q, x);
+    dq = flip_neg_(dq, d_sign);
+    q = add_(abs_(d_sign), c.one);
+  }
   const L x2 = mul_(x, x);
   L r = rcp_(q);
   if constexpr (kRefine) {  // Newton-Raphson: r <- r + r (1 - q r)
@@ -392,7 +453,8 @@ __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[k
   const L u = mul_(go, r);            // go / Q
   const L y = mul_(p, r);             // P / Q
   const L t = fma_(neg_(y), dq, dp);  // P' - y Q'
-  const L w = mul_(u, y);             // go P / Q^2
+  L w = mul_(u, y);                   // go P / Q^2
+  if constexpr (kF != kFormulaKat) w = flip_neg_(w, d_sign);  // sgn(D) go P / Q^2
   const L x3 = mul_(x2, x);
   const L x4 = mul_(x2, x2);
   const L x5 = mul_(x4, x);
@@ -410,20 +472,20 @@ __device__ __forceinline__ L bwd_math(L x, L go, const BwdCoef<L>& c, L (&acc)[k
 }
 
 // One vector through the forward / backward math.
-template <typename Tio, int V, typename L, bool kExact>
+template <typename Tio, int V, typename L, bool kExact, int kF = kFormulaKat>
 __device__ __forceinline__ typename RawOf<Tio, V>::T fwd_vec(typename RawOf<Tio, V>::T raw,
                                                              const FwdCoef<L>& c) {
   Frag<V> f = unpack<Tio, V>(raw);
   if constexpr (V == 1) {
-    f.s = fwd_math<float, kExact>(f.s, c);
+    f.s = fwd_math<float, kExact, kF>(f.s, c);
   } else {
 #pragma unroll
-    for (int k = 0; k < V / 2; ++k) f.p[k] = fwd_math<float2, kExact>(f.p[k], c);
+    for (int k = 0; k < V / 2; ++k) f.p[k] = fwd_math<float2, kExact, kF>(f.p[k], c);
   }
   return pack<Tio, V>(f);
 }
 
-template <typename Tio, int V, typename L, bool kRefine>
+template <typename Tio, int V, typename L, bool kRefine, int kF = kFormulaKat>
 __device__ __forceinline__ typename RawOf<Tio, V>::T bwd_vec(typename RawOf<Tio, V>::T rx,
                                                              typename RawOf<Tio, V>::T rg,
                                                              const BwdCoef<L>& c,
@@ -431,10 +493,11 @@ __device__ __forceinline__ typename RawOf<Tio, V>::T bwd_vec(typename RawOf<Tio,
   Frag<V> fx = unpack<Tio, V>(rx);
   const Frag<V> fg = unpack<Tio, V>(rg);
   if constexpr (V == 1) {
-    fx.s = bwd_math<float, kRefine>(fx.s, fg.s, c, acc);
+    fx.s = bwd_math<float, kRefine, kF>(fx.s, fg.s, c, acc);
   } else {
 #pragma unroll
-    for (int k = 0; k < V / 2; ++k) fx.p[k] = bwd_math<float2, kRefine>(fx.p[k], fg.p[k], c, acc);
+    for (int k = 0; k < V / 2; ++k)
+      fx.p[k] = from_lane(bwd_math<L, kRefine, kF>(to_lane<L>(fx.p[k]), to_lane<L>(fg.p[k]), c, acc));
   }
   return pack<Tio, V>(fx);
 }
@@ -524,7 +587,7 @@ __device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float*
 // Rows handled by thread row `tr` inside a segment start at r0 and step by tile_rows;
 // they are processed U at a time, and the next U rows are loaded before the current
 // ones are computed, so every thread keeps loads in flight while it computes.
-template <typename Tio, int V, int U>
+template <typename Tio, int V, int U, int kF>
 __global__ void __launch_bounds__(kMaxThreads)
 kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
                const float* __restrict__ num, const float* __restrict__ den, const Plan p) {
@@ -545,7 +608,7 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
     const int64_t r_end = seg_end - cb * p.rows;
     if (col < p.vec_cols && r0 < r_end) {
       FwdCoef<L> c;
-      load_fwd_coef<L>(num, den, col / p.vec_group, c);
+      load_fwd_coef<L, kF>(num, den, col / p.vec_group, c);
       const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
       const Tio* xp = x + r0 * p.width + col * V;
       Tio* yp = y + r0 * p.width + col * V;
@@ -562,7 +625,8 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
           if (b + U + u < n) nxt[u] = load_raw<Tio, V>(xp + u * step);
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (b + u < n) store_raw<Tio, V>(yp + u * step, fwd_vec<Tio, V, L, kExact>(cur[u], c));
+          if (b + u < n)
+            store_raw<Tio, V>(yp + u * step, fwd_vec<Tio, V, L, kExact, kF>(cur[u], c));
 #pragma unroll
         for (int u = 0; u < U; ++u) cur[u] = nxt[u];
         xp += U * step;
@@ -577,7 +641,7 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
 // Backward kernel (dx + per-block partial coefficient sums).
 // ---------------------------------------------------------------------------
 
-template <typename Tio, int V, int U>
+template <typename Tio, int V, int U, int kF>
 __global__ void __launch_bounds__(kMaxThreads)
 kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
                const float* __restrict__ num, const float* __restrict__ den,
@@ -609,7 +673,7 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
     const int64_t r_end = seg_end - cb * p.rows;
     if (row_thread && col < p.vec_cols && r0 < r_end) {
       BwdCoef<L> c;
-      load_bwd_coef<L>(num, den, col / p.vec_group, c);
+      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c);
       const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
       const int64_t off = r0 * p.width + col * V;
       const Tio* xp = x + off;
@@ -638,7 +702,7 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           if (b + u < n) {
-            const Raw d = bwd_vec<Tio, V, L, kRefine>(cx[u], cg[u], c, acc);
+            const Raw d = bwd_vec<Tio, V, L, kRefine, kF>(cx[u], cg[u], c, acc);
             if (write_dx) store_raw<Tio, V>(dp + u * step, d);
           }
         }
@@ -697,13 +761,14 @@ __device__ __forceinline__ void cp_async_wait() {
 #define KAT_ASYNC_BOUNDS __launch_bounds__(kMaxThreads)
 #endif
 
-template <typename Tio, int kStages, int kRows>
+template <typename Tio, int kStages, int kRows, int kF>
 __global__ void KAT_ASYNC_BOUNDS
 kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
                      const float* __restrict__ num, const float* __restrict__ den,
                      double* __restrict__ partial, const Plan p) {
   constexpr int V = 16 / sizeof(Tio);
   constexpr bool kRefine = sizeof(Tio) == 4;
+  using L = typename std::conditional<sizeof(Tio) == 4, S2, float2>::type;
   extern __shared__ __align__(16) uint4 ring[];
   const int T = blockDim.x;
   float* s_acc = reinterpret_cast<float*>(ring + size_t(kStages) * kRows * 2 * T);
@@ -726,12 +791,12 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
     const int64_t col = cb * p.tile_cols + tc;
     const int64_t r0 = i - cb * p.rows + tr;
     const int64_t r_end = seg_end - cb * p.rows;
-    float2 acc[kAcc];
+    L acc[kAcc];
 #pragma unroll
-    for (int k = 0; k < kAcc; ++k) acc[k] = make_float2(0.0f, 0.0f);
+    for (int k = 0; k < kAcc; ++k) acc[k] = bcast<L>(0.0f);
     if (row_thread && col < p.vec_cols && r0 < r_end) {
-      BwdCoef<float2> c;
-      load_bwd_coef<float2>(num, den, col / p.vec_group, c);
+      BwdCoef<L> c;
+      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c);
       const int n = int(min(int64_t(0x7fffffff), (r_end - r0 + p.tile_rows - 1) / p.tile_rows));
       const int nb = (n + kRows - 1) / kRows;
       const int64_t off = r0 * p.width + col * V;
@@ -769,7 +834,7 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
           if (b * kRows + u < n) {
             const uint4 rx = sp[u * slot_stride];
             const uint4 rg = sp[u * slot_stride + T];
-            const uint4 d = bwd_vec<Tio, V, float2, kRefine>(rx, rg, c, acc);
+            const uint4 d = bwd_vec<Tio, V, L, kRefine, kF>(rx, rg, c, acc);
             if (write_dx) {
               store_raw<Tio, V>(dp, d);
               dp += step;
@@ -820,11 +885,13 @@ __device__ __forceinline__ void group_totals(const double* __restrict__ partial,
   }
 }
 
-// Writes one group's gradients from its totals: d_num = sums, d_den = -sgn(b) * sums (with
-// sgn(0) = 0 and sgn(NaN) = NaN, as torch.sgn).  Lane k < 10 writes slot k.
+// Writes one group's gradients from its totals: d_num = sums; d_den = -sgn(b) * sums for
+// the KAT formula (sgn(0) = 0 and sgn(NaN) = NaN, as torch.sgn), -sums for the abs-after-sum
+// formula (whose per-element sign was applied in the sums).  Lane k < 10 writes slot k.
 __device__ __forceinline__ void write_group(const double (&tot)[kAcc], double scale, bool ok,
                                             int64_t g, int lane, const float* __restrict__ den,
-                                            float* __restrict__ dnum, float* __restrict__ dden) {
+                                            float* __restrict__ dnum, float* __restrict__ dden,
+                                            int formula) {
   double v = 0.0;
 #pragma unroll
   for (int k = 0; k < kAcc; ++k)
@@ -834,8 +901,11 @@ __device__ __forceinline__ void write_group(const double (&tot)[kAcc], double sc
   if (lane < 6) {
     dnum[g * 6 + lane] = f;
   } else {
-    const float b = den[g * 4 + (lane - 6)];
-    const float sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
+    float sg = 1.0f;
+    if (formula == kFormulaKat) {
+      const float b = den[g * 4 + (lane - 6)];
+      sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
+    }
     dden[g * 4 + (lane - 6)] = -(sg * f);
   }
 }
@@ -850,7 +920,7 @@ kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restric
   if (g >= p.num_groups) return;
   double tot[kAcc];
   group_totals(partial, p, g, lane, tot);
-  write_group(tot, 1.0, true, g, lane, den, dnum, dden);
+  write_group(tot, 1.0, true, g, lane, den, dnum, dden, p.formula);
 }
 
 // ---------------------------------------------------------------------------
@@ -1074,7 +1144,7 @@ kat_fwd_tma_kernel(const Tio* __restrict__ x, Tio* __restrict__ y, const float* 
     const int64_t col = cb * p.tile_cols + tc;
     if (row_thread && col < p.vec_cols) {
       if (cb != cb_coef) {
-        load_fwd_coef<float2>(num, den, col / p.vec_group, c);
+        load_fwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c);
         cb_coef = cb;
       }
       const char* src = slots + size_t(s) * slot_bytes + size_t(tc) * 16;
@@ -1137,7 +1207,7 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
     const int64_t col = cb * p.tile_cols + tc;
     if (row_thread && col < p.vec_cols) {
       if (cb != cb_coef) {
-        load_bwd_coef<float2>(num, den, col / p.vec_group, c);
+        load_bwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c);
         cb_coef = cb;
       }
       const char* xs = slots + (size_t(s) * 2) * slot_bytes + size_t(tc) * 16;
@@ -1279,7 +1349,7 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
       for (int q = 0; q < peers.world; ++q) v += inbox[size_t(q) * n_out + g * kAcc + k];
       tot[k] = v;
     }
-    write_group(tot, scale, s_ok != 0, g, lane, den, dnum, dden);
+    write_group(tot, scale, s_ok != 0, g, lane, den, dnum, dden, p.formula);
   }
 }
 
@@ -1433,55 +1503,67 @@ cudaError_t kernel_occupancy(int dev, const void* fn, int threads, int* out) {
   return cudaSuccess;
 }
 
-// Kernel selection by (dtype, vec).
-const void* fwd_kernel_for(int dtype, int vec) {
+// Kernel selection by (dtype, vec, formula).
+template <int kF>
+const void* fwd_kernel_for_f(int dtype, int vec) {
   switch (dtype) {
     case KAT_DTYPE_F32:
       switch (vec) {
-        case 4: return (const void*)kat_fwd_kernel<float, 4, kUnroll>;
-        case 2: return (const void*)kat_fwd_kernel<float, 2, kUnroll>;
-        default: return (const void*)kat_fwd_kernel<float, 1, kUnroll>;
+        case 4: return (const void*)kat_fwd_kernel<float, 4, kUnroll, kF>;
+        case 2: return (const void*)kat_fwd_kernel<float, 2, kUnroll, kF>;
+        default: return (const void*)kat_fwd_kernel<float, 1, kUnroll, kF>;
       }
     case KAT_DTYPE_F16:
       switch (vec) {
-        case 8: return (const void*)kat_fwd_kernel<__half, 8, kUnroll>;
-        case 4: return (const void*)kat_fwd_kernel<__half, 4, kUnroll>;
-        case 2: return (const void*)kat_fwd_kernel<__half, 2, kUnroll>;
-        default: return (const void*)kat_fwd_kernel<__half, 1, kUnroll>;
+        case 8: return (const void*)kat_fwd_kernel<__half, 8, kUnroll, kF>;
+        case 4: return (const void*)kat_fwd_kernel<__half, 4, kUnroll, kF>;
+        case 2: return (const void*)kat_fwd_kernel<__half, 2, kUnroll, kF>;
+        default: return (const void*)kat_fwd_kernel<__half, 1, kUnroll, kF>;
       }
     default:
       switch (vec) {
-        case 8: return (const void*)kat_fwd_kernel<__nv_bfloat16, 8, kUnroll>;
-        case 4: return (const void*)kat_fwd_kernel<__nv_bfloat16, 4, kUnroll>;
-        case 2: return (const void*)kat_fwd_kernel<__nv_bfloat16, 2, kUnroll>;
-        default: return (const void*)kat_fwd_kernel<__nv_bfloat16, 1, kUnroll>;
+        case 8: return (const void*)kat_fwd_kernel<__nv_bfloat16, 8, kUnroll, kF>;
+        case 4: return (const void*)kat_fwd_kernel<__nv_bfloat16, 4, kUnroll, kF>;
+        case 2: return (const void*)kat_fwd_kernel<__nv_bfloat16, 2, kUnroll, kF>;
+        default: return (const void*)kat_fwd_kernel<__nv_bfloat16, 1, kUnroll, kF>;
       }
   }
 }
 
-const void* bwd_kernel_for(int dtype, int vec) {
+template <int kF>
+const void* bwd_kernel_for_f(int dtype, int vec) {
   switch (dtype) {
     case KAT_DTYPE_F32:
       switch (vec) {
-        case 4: return (const void*)kat_bwd_kernel<float, 4, kUnrollBwd>;
-        case 2: return (const void*)kat_bwd_kernel<float, 2, kUnrollBwd>;
-        default: return (const void*)kat_bwd_kernel<float, 1, kUnrollBwd>;
+        case 4: return (const void*)kat_bwd_kernel<float, 4, kUnrollBwd, kF>;
+        case 2: return (const void*)kat_bwd_kernel<float, 2, kUnrollBwd, kF>;
+        default: return (const void*)kat_bwd_kernel<float, 1, kUnrollBwd, kF>;
       }
     case KAT_DTYPE_F16:
       switch (vec) {
-        case 8: return (const void*)kat_bwd_kernel<__half, 8, kUnrollBwd>;
-        case 4: return (const void*)kat_bwd_kernel<__half, 4, kUnrollBwd>;
-        case 2: return (const void*)kat_bwd_kernel<__half, 2, kUnrollBwd>;
-        default: return (const void*)kat_bwd_kernel<__half, 1, kUnrollBwd>;
+        case 8: return (const void*)kat_bwd_kernel<__half, 8, kUnrollBwd, kF>;
+        case 4: return (const void*)kat_bwd_kernel<__half, 4, kUnrollBwd, kF>;
+        case 2: return (const void*)kat_bwd_kernel<__half, 2, kUnrollBwd, kF>;
+        default: return (const void*)kat_bwd_kernel<__half, 1, kUnrollBwd, kF>;
       }
     default:
       switch (vec) {
-        case 8: return (const void*)kat_bwd_kernel<__nv_bfloat16, 8, kUnrollBwd>;
-        case 4: return (const void*)kat_bwd_kernel<__nv_bfloat16, 4, kUnrollBwd>;
-        case 2: return (const void*)kat_bwd_kernel<__nv_bfloat16, 2, kUnrollBwd>;
-        default: return (const void*)kat_bwd_kernel<__nv_bfloat16, 1, kUnrollBwd>;
+        case 8: return (const void*)kat_bwd_kernel<__nv_bfloat16, 8, kUnrollBwd, kF>;
+        case 4: return (const void*)kat_bwd_kernel<__nv_bfloat16, 4, kUnrollBwd, kF>;
+        case 2: return (const void*)kat_bwd_kernel<__nv_bfloat16, 2, kUnrollBwd, kF>;
+        default: return (const void*)kat_bwd_kernel<__nv_bfloat16, 1, kUnrollBwd, kF>;
       }
   }
+}
+
+const void* fwd_kernel_for(int dtype, int vec, int formula) {
+  return formula == kFormulaKat ? fwd_kernel_for_f<kFormulaKat>(dtype, vec)
+                                : fwd_kernel_for_f<kFormulaAbsSum>(dtype, vec);
+}
+
+const void* bwd_kernel_for(int dtype, int vec, int formula) {
+  return formula == kFormulaKat ? bwd_kernel_for_f<kFormulaKat>(dtype, vec)
+                                : bwd_kernel_for_f<kFormulaAbsSum>(dtype, vec);
 }
 
 // Widest vector the shape and every (non-NULL) pointer allow.
@@ -1568,62 +1650,78 @@ int plan_for_launch_uncached(const void* fn, int64_t batch, int64_t channels, in
   return make_plan_impl(batch, channels, inner, num_groups, dtype, vec, sms, occ, p);
 }
 
-template <typename Tio, int V>
+template <typename Tio, int V, int kF>
 cudaError_t launch_fwd_t(const void* x, void* y, const float* num, const float* den, const Plan& p,
                          cudaStream_t s) {
-  kat_fwd_kernel<Tio, V, kUnroll><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
+  kat_fwd_kernel<Tio, V, kUnroll, kF><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
       static_cast<const Tio*>(x), static_cast<Tio*>(y), num, den, p);
   return cudaGetLastError();
 }
 
-template <typename Tio, int V>
+template <typename Tio, int V, int kF>
 cudaError_t launch_bwd_t(const void* x, const void* gy, void* dx, const float* num,
                          const float* den, double* partial, const Plan& p, cudaStream_t s) {
-  kat_bwd_kernel<Tio, V, kUnrollBwd><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
+  kat_bwd_kernel<Tio, V, kUnrollBwd, kF><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
       static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num, den,
       partial, p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_fwd(int dtype, int vec, const void* x, void* y, const float* num,
+template <int kF>
+cudaError_t launch_fwd_f(int dtype, int vec, const void* x, void* y, const float* num,
                        const float* den, const Plan& p, cudaStream_t s) {
   switch (dtype) {
     case KAT_DTYPE_F32:
-      if (vec == 4) return launch_fwd_t<float, 4>(x, y, num, den, p, s);
-      if (vec == 2) return launch_fwd_t<float, 2>(x, y, num, den, p, s);
-      return launch_fwd_t<float, 1>(x, y, num, den, p, s);
+      if (vec == 4) return launch_fwd_t<float, 4, kF>(x, y, num, den, p, s);
+      if (vec == 2) return launch_fwd_t<float, 2, kF>(x, y, num, den, p, s);
+      return launch_fwd_t<float, 1, kF>(x, y, num, den, p, s);
     case KAT_DTYPE_F16:
-      if (vec == 8) return launch_fwd_t<__half, 8>(x, y, num, den, p, s);
-      if (vec == 4) return launch_fwd_t<__half, 4>(x, y, num, den, p, s);
-      if (vec == 2) return launch_fwd_t<__half, 2>(x, y, num, den, p, s);
-      return launch_fwd_t<__half, 1>(x, y, num, den, p, s);
+      if (vec == 8) return launch_fwd_t<__half, 8, kF>(x, y, num, den, p, s);
+      if (vec == 4) return launch_fwd_t<__half, 4, kF>(x, y, num, den, p, s);
+      if (vec == 2) return launch_fwd_t<__half, 2, kF>(x, y, num, den, p, s);
+      return launch_fwd_t<__half, 1, kF>(x, y, num, den, p, s);
     default:
-      if (vec == 8) return launch_fwd_t<__nv_bfloat16, 8>(x, y, num, den, p, s);
-      if (vec == 4) return launch_fwd_t<__nv_bfloat16, 4>(x, y, num, den, p, s);
-      if (vec == 2) return launch_fwd_t<__nv_bfloat16, 2>(x, y, num, den, p, s);
-      return launch_fwd_t<__nv_bfloat16, 1>(x, y, num, den, p, s);
+      if (vec == 8) return launch_fwd_t<__nv_bfloat16, 8, kF>(x, y, num, den, p, s);
+      if (vec == 4) return launch_fwd_t<__nv_bfloat16, 4, kF>(x, y, num, den, p, s);
+      if (vec == 2) return launch_fwd_t<__nv_bfloat16, 2, kF>(x, y, num, den, p, s);
+      return launch_fwd_t<__nv_bfloat16, 1, kF>(x, y, num, den, p, s);
   }
 }
 
-cudaError_t launch_bwd(int dtype, int vec, const void* x, const void* gy, void* dx,
+template <int kF>
+cudaError_t launch_bwd_f(int dtype, int vec, const void* x, const void* gy, void* dx,
                        const float* num, const float* den, double* partial, const Plan& p,
                        cudaStream_t s) {
   switch (dtype) {
     case KAT_DTYPE_F32:
-      if (vec == 4) return launch_bwd_t<float, 4>(x, gy, dx, num, den, partial, p, s);
-      if (vec == 2) return launch_bwd_t<float, 2>(x, gy, dx, num, den, partial, p, s);
-      return launch_bwd_t<float, 1>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 4) return launch_bwd_t<float, 4, kF>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 2) return launch_bwd_t<float, 2, kF>(x, gy, dx, num, den, partial, p, s);
+      return launch_bwd_t<float, 1, kF>(x, gy, dx, num, den, partial, p, s);
     case KAT_DTYPE_F16:
-      if (vec == 8) return launch_bwd_t<__half, 8>(x, gy, dx, num, den, partial, p, s);
-      if (vec == 4) return launch_bwd_t<__half, 4>(x, gy, dx, num, den, partial, p, s);
-      if (vec == 2) return launch_bwd_t<__half, 2>(x, gy, dx, num, den, partial, p, s);
-      return launch_bwd_t<__half, 1>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 8) return launch_bwd_t<__half, 8, kF>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 4) return launch_bwd_t<__half, 4, kF>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 2) return launch_bwd_t<__half, 2, kF>(x, gy, dx, num, den, partial, p, s);
+      return launch_bwd_t<__half, 1, kF>(x, gy, dx, num, den, partial, p, s);
     default:
-      if (vec == 8) return launch_bwd_t<__nv_bfloat16, 8>(x, gy, dx, num, den, partial, p, s);
-      if (vec == 4) return launch_bwd_t<__nv_bfloat16, 4>(x, gy, dx, num, den, partial, p, s);
-      if (vec == 2) return launch_bwd_t<__nv_bfloat16, 2>(x, gy, dx, num, den, partial, p, s);
-      return launch_bwd_t<__nv_bfloat16, 1>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 8) return launch_bwd_t<__nv_bfloat16, 8, kF>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 4) return launch_bwd_t<__nv_bfloat16, 4, kF>(x, gy, dx, num, den, partial, p, s);
+      if (vec == 2) return launch_bwd_t<__nv_bfloat16, 2, kF>(x, gy, dx, num, den, partial, p, s);
+      return launch_bwd_t<__nv_bfloat16, 1, kF>(x, gy, dx, num, den, partial, p, s);
   }
+}
+
+cudaError_t launch_fwd(int dtype, int vec, int formula, const void* x, void* y,
+                       const float* num, const float* den, const Plan& p, cudaStream_t s) {
+  return formula == kFormulaKat ? launch_fwd_f<kFormulaKat>(dtype, vec, x, y, num, den, p, s)
+                                : launch_fwd_f<kFormulaAbsSum>(dtype, vec, x, y, num, den, p, s);
+}
+
+cudaError_t launch_bwd(int dtype, int vec, int formula, const void* x, const void* gy, void* dx,
+                       const float* num, const float* den, double* partial, const Plan& p,
+                       cudaStream_t s) {
+  return formula == kFormulaKat
+             ? launch_bwd_f<kFormulaKat>(dtype, vec, x, gy, dx, num, den, partial, p, s)
+             : launch_bwd_f<kFormulaAbsSum>(dtype, vec, x, gy, dx, num, den, partial, p, s);
 }
 
 // ----- Bulk-copy pipeline: planning and launch --------------------------------
@@ -1815,29 +1913,37 @@ size_t async_smem_bytes(int threads) {
   return size_t(kAsyncStages) * kAsyncRows * 2 * 16 * threads + size_t(kAcc) * 4 * (threads + 1);
 }
 
-const void* bwd_async_kernel_for(int dtype) {
+template <int kF>
+const void* bwd_async_kernel_for_f(int dtype) {
   switch (dtype) {
-    case KAT_DTYPE_F32: return (const void*)kat_bwd_async_kernel<float, kAsyncStages, kAsyncRows>;
-    case KAT_DTYPE_F16: return (const void*)kat_bwd_async_kernel<__half, kAsyncStages, kAsyncRows>;
-    default: return (const void*)kat_bwd_async_kernel<__nv_bfloat16, kAsyncStages, kAsyncRows>;
+    case KAT_DTYPE_F32: return (const void*)kat_bwd_async_kernel<float, kAsyncStages, kAsyncRows, kF>;
+    case KAT_DTYPE_F16:
+      return (const void*)kat_bwd_async_kernel<__half, kAsyncStages, kAsyncRows, kF>;
+    default: return (const void*)kat_bwd_async_kernel<__nv_bfloat16, kAsyncStages, kAsyncRows, kF>;
   }
+}
+
+const void* bwd_async_kernel_for(int dtype, int formula) {
+  return formula == kFormulaKat ? bwd_async_kernel_for_f<kFormulaKat>(dtype)
+                                : bwd_async_kernel_for_f<kFormulaAbsSum>(dtype);
 }
 
 // Plan of the cp.async backward: occupancy from the kernel's registers and its shared
 // memory at this block size.  Returns -1 when it does not apply.
 int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
-                        int dtype, int* dev_out, Plan* p);
+                        int dtype, int formula, int* dev_out, Plan* p);
 
 int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-               int* dev_out, Plan* p) {
+               int formula, int* dev_out, Plan* p) {
   if (pipeline_mode() != 0) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
-  const PlanKey key{dev, bwd_async_kernel_for(dtype), dtype, max_vec_for(dtype), batch, channels,
+  const PlanKey key{dev, bwd_async_kernel_for(dtype, formula), dtype, max_vec_for(dtype), batch, channels,
                     inner, num_groups};
   PlanEntry e;
   if (!plan_cache_get(key, &e)) {
-    e.status = plan_async_uncached(batch, channels, inner, num_groups, dtype, dev_out, &e.plan);
+    e.status = plan_async_uncached(batch, channels, inner, num_groups, dtype, formula, dev_out,
+                                   &e.plan);
     if (e.status == KAT_OK || e.status == -1) plan_cache_put(key, e);
   }
   *dev_out = dev;
@@ -1846,7 +1952,7 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
 }
 
 int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
-                        int dtype, int* dev_out, Plan* p) {
+                        int dtype, int formula, int* dev_out, Plan* p) {
   const int vmax = max_vec_for(dtype);
   const int64_t gw = (channels / num_groups) * inner;
   if (pipeline_mode() != 0 || gw % vmax != 0) return -1;
@@ -1862,7 +1968,7 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
   int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
                           max_cols);
   if (st != KAT_OK) return st;
-  const void* fn = bwd_async_kernel_for(dtype);
+  const void* fn = bwd_async_kernel_for(dtype, formula);
   const size_t smem = async_smem_bytes(probe.threads);
   if (smem > size_t(kPipeSmemBudget)) return -1;
   if (allow_dynamic_smem(dev, fn, uint32_t(smem)) != cudaSuccess) return KAT_ERR_CUDA;
@@ -1886,23 +1992,33 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
   return st;
 }
 
-template <typename Tio>
+template <typename Tio, int kF>
 cudaError_t launch_bwd_async_t(const void* x, const void* gy, void* dx, const float* num,
                                const float* den, double* partial, const Plan& p, cudaStream_t s) {
-  kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows>
+  kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows, kF>
       <<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), async_smem_bytes(p.threads), s>>>(
           static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num,
           den, partial, p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_bwd_async(int dtype, const void* x, const void* gy, void* dx, const float* num,
-                             const float* den, double* partial, const Plan& p, cudaStream_t s) {
+template <int kF>
+cudaError_t launch_bwd_async_f(int dtype, const void* x, const void* gy, void* dx,
+                               const float* num, const float* den, double* partial, const Plan& p,
+                               cudaStream_t s) {
   switch (dtype) {
-    case KAT_DTYPE_F32: return launch_bwd_async_t<float>(x, gy, dx, num, den, partial, p, s);
-    case KAT_DTYPE_F16: return launch_bwd_async_t<__half>(x, gy, dx, num, den, partial, p, s);
-    default: return launch_bwd_async_t<__nv_bfloat16>(x, gy, dx, num, den, partial, p, s);
+    case KAT_DTYPE_F32: return launch_bwd_async_t<float, kF>(x, gy, dx, num, den, partial, p, s);
+    case KAT_DTYPE_F16: return launch_bwd_async_t<__half, kF>(x, gy, dx, num, den, partial, p, s);
+    default: return launch_bwd_async_t<__nv_bfloat16, kF>(x, gy, dx, num, den, partial, p, s);
   }
+}
+
+cudaError_t launch_bwd_async(int dtype, int formula, const void* x, const void* gy, void* dx,
+                             const float* num, const float* den, double* partial, const Plan& p,
+                             cudaStream_t s) {
+  return formula == kFormulaKat
+             ? launch_bwd_async_f<kFormulaKat>(dtype, x, gy, dx, num, den, partial, p, s)
+             : launch_bwd_async_f<kFormulaAbsSum>(dtype, x, gy, dx, num, den, partial, p, s);
 }
 
 cudaError_t launch_fwd_tma(int dtype, const void* x, void* y, const float* num, const float* den,
@@ -1949,10 +2065,12 @@ int launch_reduce(const void* workspace, const float* den, float* dnum, float* d
 int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* numerator,
              const float* denominator, float* grad_numerator, float* grad_denominator,
              void* workspace, size_t workspace_bytes, int64_t batch, int64_t channels,
-             int64_t inner, int64_t num_groups, int dtype, void* stream, const Peers* peers) {
+             int64_t inner, int64_t num_groups, int dtype, int formula, void* stream,
+             const Peers* peers) {
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
+  if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
   if (numerator == nullptr || denominator == nullptr || grad_numerator == nullptr ||
       grad_denominator == nullptr)
     return KAT_ERR_NULL_POINTER;
@@ -1965,19 +2083,21 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
   Plan p;
   if (n != 0 && vec == max_vec_for(dtype)) {
     int dev = 0;
-    st = plan_async(batch, channels, inner, num_groups, dtype, &dev, &p);
+    st = plan_async(batch, channels, inner, num_groups, dtype, formula, &dev, &p);
     if (st != -1) {
       if (st != KAT_OK) return st;
       if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
           (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
         return KAT_ERR_WORKSPACE;
-      if (launch_bwd_async(dtype, x, grad_out, grad_x, numerator, denominator,
+      if (launch_bwd_async(dtype, formula, x, grad_out, grad_x, numerator, denominator,
                            static_cast<double*>(workspace), p, s) != cudaSuccess)
         return KAT_ERR_CUDA;
+      p.formula = formula;
       return launch_reduce(workspace, denominator, grad_numerator, grad_denominator, p, peers, s);
     }
   }
-  if (n != 0 && vec == max_vec_for(dtype)) {
+  // The bulk-copy design computes the KAT formula only.
+  if (n != 0 && vec == max_vec_for(dtype) && formula == kFormulaKat) {
     Pipe q;
     int dev = 0;
     st = plan_tma(batch, channels, inner, num_groups, dtype, true, &dev, &p, &q);
@@ -1997,18 +2117,19 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
   if (n == 0) {
     st = make_plan_impl(batch, channels, inner, num_groups, dtype, vec, 1, 1, &p);
   } else {
-    st = plan_for_launch(bwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype,
-                         vec, &p);
+    st = plan_for_launch(bwd_kernel_for(dtype, vec, formula), batch, channels, inner, num_groups,
+                         dtype, vec, &p);
   }
   if (st != KAT_OK) return st;
   if (p.blocks > 0) {
     if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
         (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
       return KAT_ERR_WORKSPACE;
-    if (launch_bwd(dtype, vec, x, grad_out, grad_x, numerator, denominator,
+    if (launch_bwd(dtype, vec, formula, x, grad_out, grad_x, numerator, denominator,
                    static_cast<double*>(workspace), p, s) != cudaSuccess)
       return KAT_ERR_CUDA;
   }
+  p.formula = formula;
   return launch_reduce(workspace, denominator, grad_numerator, grad_denominator, p, peers, s);
 }
 
@@ -2030,6 +2151,8 @@ const char* kat_rational_strerror(int status) {
     case KAT_ERR_BAD_GROUPS: return "num_groups must be >= 1 and divide channels";
     case KAT_ERR_WORKSPACE: return "workspace is NULL, misaligned or smaller than required";
     case KAT_ERR_CUDA: return "CUDA runtime or kernel launch error";
+    case KAT_ERR_BAD_FORMULA:
+      return "unsupported formula (expected KAT_FORMULA_KAT or KAT_FORMULA_ABS_SUM)";
     case KAT_ERR_SCRATCH_LIMIT:
       return "problem needs more backward scratch than kat_rational_bwd_noalloc's fixed "
              "2 MiB device buffer holds; use kat_rational_bwd with a caller-allocated workspace";
@@ -2068,12 +2191,79 @@ int kat_rational_make_plan(int64_t batch, int64_t channels, int64_t inner, int64
   return KAT_OK;
 }
 
-int kat_rational_fwd(const void* x, void* y, const float* numerator, const float* denominator,
-                     int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-                     void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Float64 forward, for float64 tensors (gradient checking).  One element per thread in a
+// grid-stride loop; the group of element i is ((i / inner) % channels) / (channels / G).
+// Coefficients are float64 as well, and the arithmetic is float64 throughout (fma Horner,
+// IEEE division), as the reference's Triton forward computes in its input dtype.
+template <int kF>
+__global__ void __launch_bounds__(256)
+kat_fwd_f64_kernel(const double* __restrict__ x, double* __restrict__ y,
+                   const double* __restrict__ num, const double* __restrict__ den, int64_t n,
+                   int64_t inner, int64_t channels, int64_t per_group) {
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int64_t g = ((i / inner) % channels) / per_group;
+    const double* a = num + g * 6;
+    const double* b = den + g * 4;
+    const double v = x[i];
+    double p = fma(a[5], v, a[4]);
+    p = fma(p, v, a[3]);
+    p = fma(p, v, a[2]);
+    p = fma(p, v, a[1]);
+    p = fma(p, v, a[0]);
+    double q;
+    if constexpr (kF == kFormulaKat) {
+      q = fma(fabs(b[3]), v, fabs(b[2]));
+      q = fma(q, v, fabs(b[1]));
+      q = fma(q, v, fabs(b[0]));
+      q = fma(q, v, 1.0);
+    } else {
+      q = fma(b[3], v, b[2]);
+      q = fma(q, v, b[1]);
+      q = fma(q, v, b[0]);
+      q = 1.0 + fabs(q * v);
+    }
+    y[i] = p / q;
+  }
+}
+
+int fwd_f64_impl(const double* x, double* y, const double* numerator, const double* denominator,
+                 int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int formula,
+                 void* stream) {
+  int64_t n = 0;
+  int st = validate_dims(batch, channels, inner, num_groups, KAT_DTYPE_F32, &n);
+  if (st != KAT_OK) return st;
+  if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
+  if (numerator == nullptr || denominator == nullptr) return KAT_ERR_NULL_POINTER;
+  if (n == 0) return KAT_OK;
+  if (x == nullptr || y == nullptr) return KAT_ERR_NULL_POINTER;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || device_sm_count(dev, &sms) != cudaSuccess)
+    return KAT_ERR_CUDA;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, int64_t(sms) * 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t per_group = channels / num_groups;
+  if (formula == kFormulaKat) {
+    kat_fwd_f64_kernel<kFormulaKat><<<unsigned(blocks), 256, 0, s>>>(
+        x, y, numerator, denominator, n, inner, channels, per_group);
+  } else {
+    kat_fwd_f64_kernel<kFormulaAbsSum><<<unsigned(blocks), 256, 0, s>>>(
+        x, y, numerator, denominator, n, inner, channels, per_group);
+  }
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+int fwd_impl(const void* x, void* y, const float* numerator, const float* denominator,
+             int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
+             int formula, void* stream) {
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
+  if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
   if (numerator == nullptr || denominator == nullptr) return KAT_ERR_NULL_POINTER;
   if (n == 0) return KAT_OK;
   if (x == nullptr || y == nullptr) return KAT_ERR_NULL_POINTER;
@@ -2081,7 +2271,7 @@ int kat_rational_fwd(const void* x, void* y, const float* numerator, const float
   const void* ptrs[2] = {x, y};
   const int vec = pick_vec(dtype, gw, ptrs, 2);
   Plan p;
-  if (vec == max_vec_for(dtype)) {
+  if (vec == max_vec_for(dtype) && formula == kFormulaKat) {
     Pipe q;
     int dev = 0;
     st = plan_tma(batch, channels, inner, num_groups, dtype, false, &dev, &p, &q);
@@ -2095,13 +2285,39 @@ int kat_rational_fwd(const void* x, void* y, const float* numerator, const float
       return KAT_OK;
     }
   }
-  st = plan_for_launch(fwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype, vec,
-                       &p);
+  st = plan_for_launch(fwd_kernel_for(dtype, vec, formula), batch, channels, inner, num_groups,
+                       dtype, vec, &p);
   if (st != KAT_OK) return st;
-  if (launch_fwd(dtype, vec, x, y, numerator, denominator, p,
+  if (launch_fwd(dtype, vec, formula, x, y, numerator, denominator, p,
                  static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return KAT_ERR_CUDA;
   return KAT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kat_rational_fwd(const void* x, void* y, const float* numerator, const float* denominator,
+                     int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
+                     void* stream) {
+  return fwd_impl(x, y, numerator, denominator, batch, channels, inner, num_groups, dtype,
+                  kFormulaKat, stream);
+}
+
+int kat_rational_fwd_f64(const double* x, double* y, const double* numerator,
+                         const double* denominator, int64_t batch, int64_t channels,
+                         int64_t inner, int64_t num_groups, int formula, void* stream) {
+  return fwd_f64_impl(x, y, numerator, denominator, batch, channels, inner, num_groups, formula,
+                      stream);
+}
+
+int kat_rational_fwd_formula(const void* x, void* y, const float* numerator,
+                             const float* denominator, int64_t batch, int64_t channels,
+                             int64_t inner, int64_t num_groups, int dtype, int formula,
+                             void* stream) {
+  return fwd_impl(x, y, numerator, denominator, batch, channels, inner, num_groups, dtype,
+                  formula, stream);
 }
 
 int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inner,
@@ -2124,17 +2340,21 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
     const int t = plan_tma(batch, channels, inner, num_groups, dtype, true, &d, &p, &q);
     if (t == KAT_OK) need = p.workspace_bytes;
     else if (t != -1) st = t;
-    const int a = st == KAT_OK ? plan_async(batch, channels, inner, num_groups, dtype, &d, &p) : -1;
-    if (a == KAT_OK) need = std::max<uint64_t>(need, p.workspace_bytes);
-    else if (a != -1) st = a;
+    for (int f = kFormulaKat; st == KAT_OK && f <= kFormulaAbsSum; ++f) {
+      const int a = plan_async(batch, channels, inner, num_groups, dtype, f, &d, &p);
+      if (a == KAT_OK) need = std::max<uint64_t>(need, p.workspace_bytes);
+      else if (a != -1) st = a;
+    }
   }
+  // Enough for every kernel the backward may pick, for either formula.
   for (int vec = max_vec_for(dtype); st == KAT_OK && vec >= 1; vec >>= 1) {
     if (gw % vec != 0) continue;
-    Plan p;
-    st = plan_for_launch(bwd_kernel_for(dtype, vec), batch, channels, inner, num_groups, dtype, vec,
-                         &p);
-    if (st != KAT_OK) break;
-    if (p.workspace_bytes > need) need = p.workspace_bytes;
+    for (int f = kFormulaKat; st == KAT_OK && f <= kFormulaAbsSum; ++f) {
+      Plan p;
+      st = plan_for_launch(bwd_kernel_for(dtype, vec, f), batch, channels, inner, num_groups,
+                           dtype, vec, &p);
+      if (st == KAT_OK && p.workspace_bytes > need) need = p.workspace_bytes;
+    }
   }
   if (device != prev) cudaSetDevice(prev);
   if (st != KAT_OK) return st;
@@ -2147,8 +2367,19 @@ int kat_rational_bwd(const void* x, const void* grad_out, void* grad_x, const fl
                      void* workspace, size_t workspace_bytes, int64_t batch, int64_t channels,
                      int64_t inner, int64_t num_groups, int dtype, void* stream) {
   return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
-                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype, stream,
-                  nullptr);
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype,
+                  kFormulaKat, stream, nullptr);
+}
+
+int kat_rational_bwd_formula(const void* x, const void* grad_out, void* grad_x,
+                             const float* numerator, const float* denominator,
+                             float* grad_numerator, float* grad_denominator, void* workspace,
+                             size_t workspace_bytes, int64_t batch, int64_t channels,
+                             int64_t inner, int64_t num_groups, int dtype, int formula,
+                             void* stream) {
+  return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype, formula,
+                  stream, nullptr);
 }
 
 int kat_rational_enable_peer_access(int device, int peer_device) {
@@ -2248,8 +2479,8 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
     pe.buf[r] = static_cast<char*>(peers->buffers[r]);
   }
   return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
-                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype, stream,
-                  &pe);
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype,
+                  kFormulaKat, stream, &pe);
 }
 
 }  // extern "C"

@@ -34,8 +34,9 @@ def _chunks(rows: int, n: int) -> List[Tuple[int, int]]:
 
 
 class HostPipeline:
-    """Forward+backward of a KAT_Group / KAT_Group2D over pinned host tensors with
-    overlapped copies.  Device buffers are kept for reuse while the input shape stays."""
+    """Forward+backward of a KAT_Group / KAT_Group2D (or a RatGroup, the abs-after-sum
+    formula) over pinned host tensors with overlapped copies.  Device buffers are kept for
+    reuse while the input shape stays."""
 
     def __init__(self, module: torch.nn.Module, chunks: int = 16, slots: int = 3,
                  device: Optional[torch.device] = None):
@@ -126,6 +127,13 @@ class HostPipeline:
             num = mod.weight_numerator.detach().float().expand(G, 6).contiguous()
             den = mod.weight_denominator.detach().float().contiguous()
         comp_ptr = ctypes.c_void_p(self.comp.cuda_stream)
+        formula = getattr(mod, "formula", _native.KAT_FORMULA_KAT)
+        if formula == _native.KAT_FORMULA_KAT:
+            fwd = lambda *a: lib.kat_rational_fwd(*a, comp_ptr)
+            bwd = lambda *a: lib.kat_rational_bwd(*a, comp_ptr)
+        else:
+            fwd = lambda *a: lib.kat_rational_fwd_formula(*a, formula, comp_ptr)
+            bwd = lambda *a: lib.kat_rational_bwd_formula(*a, formula, comp_ptr)
         ev_in, ev_comp, ev_out, used = st["ev_in"], st["ev_comp"], st["ev_out"], st["used"]
         for i, (r0, r1) in enumerate(bounds):
             k = i % self.slots
@@ -141,14 +149,13 @@ class HostPipeline:
             self.comp.wait_event(ev_in[k])
             if used[k]:
                 self.comp.wait_event(ev_out[k])       # y / dx of the slot copied out
-            _native.check("kat_rational_fwd", lib.kat_rational_fwd(
+            _native.check("kat_rational_fwd", fwd(
                 b["x"].data_ptr(), b["y"].data_ptr(), num.data_ptr(), den.data_ptr(),
-                dims[0], dims[1], dims[2], G, code, comp_ptr))
-            _native.check("kat_rational_bwd", lib.kat_rational_bwd(
+                dims[0], dims[1], dims[2], G, code))
+            _native.check("kat_rational_bwd", bwd(
                 b["x"].data_ptr(), b["g"].data_ptr(), b["dx"].data_ptr(), num.data_ptr(),
                 den.data_ptr(), st["dn"][i].data_ptr(), st["dd"][i].data_ptr(),
-                st["ws"].data_ptr(), st["ws"].numel(), dims[0], dims[1], dims[2], G, code,
-                comp_ptr))
+                st["ws"].data_ptr(), st["ws"].numel(), dims[0], dims[1], dims[2], G, code))
             ev_comp[k].record(self.comp)
             with torch.cuda.stream(self.d2h):
                 self.d2h.wait_event(ev_comp[k])
@@ -160,7 +167,7 @@ class HostPipeline:
             d_num = st["dn"][:len(bounds)].sum(dim=(0, 1)).view(1, 6)
             d_den = st["dd"][:len(bounds)].sum(dim=0)
             for p, g in ((mod.weight_numerator, d_num), (mod.weight_denominator, d_den)):
-                g = g.to(p.dtype)
+                g = g.reshape(p.shape).to(p.dtype)
                 if p.grad is None:
                     p.grad = g
                 else:

@@ -95,26 +95,53 @@ def _workspace_bytes(dims, group: int, code: int, device: torch.device) -> int:
     return out.value
 
 
-def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims) -> Tensor:
+def _fwd_f64(x: Tensor, n: Tensor, d: Tensor, group: int, dims, formula: int) -> Tensor:
+    """float64 tensors: the float64 forward kernel (kat_rational_fwd_f64)."""
+    x = x.contiguous()
+    n64 = n.detach().to(device=x.device, dtype=torch.float64).contiguous()
+    d64 = d.detach().to(device=x.device, dtype=torch.float64).contiguous()
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    with torch.cuda.device(x.device):
+        status = _native.lib().kat_rational_fwd_f64(
+            x.data_ptr(), y.data_ptr(), n64.data_ptr(), d64.data_ptr(), dims[0], dims[1],
+            dims[2], group, formula, _stream_ptr(x.device))
+    _native.check("kat_rational_fwd_f64", status)
+    return y
+
+
+def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims,
+         formula: int = _native.KAT_FORMULA_KAT) -> Tensor:
     _check_counts(n, d, group)
     _check_cuda("input", x)
+    if x.dtype == torch.float64:
+        return _fwd_f64(x, n, d, group, dims, formula)
     code = _dtype_code(x)
     x = x.contiguous()
     n32, d32 = _coefficients(n, d, group, x.device)
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
     with torch.cuda.device(x.device):
-        status = _native.lib().kat_rational_fwd(
-            x.data_ptr(), y.data_ptr(), n32.data_ptr(), d32.data_ptr(),
-            dims[0], dims[1], dims[2], group, code, _stream_ptr(x.device))
+        args = (x.data_ptr(), y.data_ptr(), n32.data_ptr(), d32.data_ptr(),
+                dims[0], dims[1], dims[2], group, code)
+        if formula == _native.KAT_FORMULA_KAT:
+            status = _native.lib().kat_rational_fwd(*args, _stream_ptr(x.device))
+        else:
+            status = _native.lib().kat_rational_fwd_formula(*args, formula,
+                                                            _stream_ptr(x.device))
     _native.check("kat_rational_fwd", status)
     return y
 
 
 def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
-         need_dx: bool = True, exchange=None):
+         need_dx: bool = True, exchange=None, formula: int = _native.KAT_FORMULA_KAT):
     _check_counts(n, d, group)
     _check_cuda("input", x)
     _check_cuda("grad_output", grad_output)
+    if x.dtype == torch.float64:
+        # float64 inputs: the fp32 backward (the reference's backward kernels compute in
+        # fp32 too), results returned in float64.
+        d_x, d_n, d_d = _bwd(grad_output.float(), x.float(), n, d, group, dims, need_dx,
+                             exchange, formula)
+        return (d_x.double() if d_x is not None else None), d_n, d_d
     code = _dtype_code(x)
     x = x.contiguous()
     if grad_output.dtype != x.dtype:
@@ -134,7 +161,12 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
                 d_x.data_ptr() if d_x is not None else None, n32.data_ptr(), d32.data_ptr(),
                 d_n.data_ptr(), d_d.data_ptr(), ws.data_ptr(), ws.numel(), dims[0], dims[1],
                 dims[2], group, code)
-        if exchange is None:
+        if exchange is not None and formula != _native.KAT_FORMULA_KAT:
+            raise ValueError("kat_rational: the fused exchange computes the KAT formula only")
+        if exchange is None and formula != _native.KAT_FORMULA_KAT:
+            status = _native.lib().kat_rational_bwd_formula(*args, formula,
+                                                            _stream_ptr(x.device))
+        elif exchange is None:
             status = _native.lib().kat_rational_bwd(*args, _stream_ptr(x.device))
         else:
             status = _native.lib().kat_rational_bwd_allreduce(

@@ -12,6 +12,9 @@ distribution and a coefficient preset, generated from fixed seeds:
                      seed 1, G=8, 'identity' coefficients
   sweep(C, G, N, dtype)  x[N/C, C] ~ N(0, 2), grad_out ~ N(0, 1), numerator [1,6] and
                      denominator [G,4] ~ N(0, 0.5) (seed 3); N rounded down to a multiple of C
+  rat_cuda_vitb_bf16 the abs-after-sum formula (rat_cuda) at the same ViT-B MLP-hidden shape
+                     x[128,197,3072] bf16 ~ N(0,1), G=8, numerator [6] and denominator [G,4]
+                     ~ N(0, 0.5) (seed 3)
 """
 
 from __future__ import annotations
@@ -39,6 +42,7 @@ class Workload:
     coef_seed: int = 2
     x_seed: int = 0
     gy_seed: int = 1
+    formula: int = 0       # 0: KAT (Q = 1 + sum |b_i| x^i), 1: abs after sum (rat_cuda)
     meta: dict = field(default_factory=dict)
 
     @property
@@ -111,10 +115,16 @@ def sweep(channels: int, groups: int, numel: int, dtype: str) -> Workload:
                     "blc", groups, dtype, "random", x_std=2.0, coef_seed=3)
 
 
+def rat_cuda_vitb_bf16() -> Workload:
+    return Workload("rat_cuda_vitb_bf16", (128, 197, 3072), "blc", 8, "bf16", "random",
+                    coef_seed=3, formula=1)
+
+
 BY_NAME = {
     "kat_group_f32": kat_group_f32,
     "kat_group_vitb_bf16": kat_group_vitb_bf16,
     "kat_group2d_f32": kat_group2d_f32,
+    "rat_cuda_vitb_bf16": rat_cuda_vitb_bf16,
 }
 
 
@@ -128,11 +138,12 @@ def get(name: str) -> Workload:
 
 def sweep_points():
     """The bandwidth-sweep points bench.py --sweep measures: C in {768, 3072, 8192},
-    G in {8, 64}, N = 2^20 .. 2^31 elements, bf16 / fp32 / fp16."""
+    G in {8, 16, 64}, N = 2^20 .. 2^30 elements, bf16 / fp32 / fp16, plus 2^31 elements at
+    C = 3072, G = 8 in bf16 and fp32."""
     pts = []
     for dt in ("bf16", "f32", "f16"):
         for c in (768, 3072, 8192):
-            for g in (8, 64):
+            for g in (8, 16, 64):
                 for logn in (20, 24, 28, 30):
                     pts.append((c, g, 1 << logn, dt))
     for dt in ("bf16", "f32"):

@@ -40,6 +40,23 @@ def test_strerror_covers_every_status():
     assert "unknown" in _native.strerror(99)
 
 
+def test_formula_entry_points_validate_before_launch():
+    lib = _native.lib()
+    assert _native.KAT_FORMULA_KAT == 0 and _native.KAT_FORMULA_ABS_SUM == 1
+    for bad in (-1, 2, 99):
+        assert lib.kat_rational_fwd_formula(1, 1, 1, 1, 4, 16, 1, 4, 0, bad, None) == \
+            _native.KAT_ERR_BAD_FORMULA
+        assert lib.kat_rational_bwd_formula(1, 1, 1, 1, 1, 1, 1, 1, 1 << 20, 4, 16, 1, 4, 0, bad,
+                                            None) == _native.KAT_ERR_BAD_FORMULA
+    # the other argument checks come first, exactly as for the KAT entry points
+    assert lib.kat_rational_fwd_formula(1, 1, 1, 1, 4, 18, 1, 4, 0, 1, None) == \
+        _native.KAT_ERR_BAD_GROUPS
+    assert lib.kat_rational_bwd_formula(1, 1, 1, 1, 1, None, 1, 1, 1 << 20, 4, 16, 1, 4, 0, 1,
+                                        None) == _native.KAT_ERR_NULL_POINTER
+    assert lib.kat_rational_fwd_formula(None, None, 1, 1, 0, 16, 1, 4, 0, 1, None) == _native.KAT_OK
+    assert "formula" in _native.strerror(_native.KAT_ERR_BAD_FORMULA)
+
+
 def _fwd(x=1, y=1, num=1, den=1, batch=4, channels=16, inner=1, groups=4, dtype=0):
     return _native.lib().kat_rational_fwd(x, y, num, den, batch, channels, inner, groups, dtype,
                                           None)

@@ -58,3 +58,41 @@ def test_host_pipeline_matches_device_call(shape, groups, dtype, layout, chunks)
     assert_coef_grads(h_grads[0], b["d_num"].sum(0, keepdims=True),
                       b["d_num_mag"].sum(0, keepdims=True), "pipeline d_num")
     assert_coef_grads(h_grads[1], b["d_den"], b["d_den_mag"], "pipeline d_den")
+
+
+def test_host_pipeline_abs_sum_formula():
+    """A RatGroup (rat_cuda's abs-after-sum formula) through the pipeline gives the same y
+    and dx as the device-resident rat_cuda call, and its coefficient gradients (numerator
+    [6], denominator [G, 4]) within 1e-4 of the float64 oracle."""
+    from oracle import rat_torch_oracle as rat
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(8)
+    G = 8
+    x = torch.randn(40, 197, 768, generator=gen).to(torch.bfloat16)
+    gy = torch.randn(40, 197, 768, generator=gen).to(torch.bfloat16)
+    a = torch.randn(6, generator=gen) * 0.5
+    b = torch.randn(G, 4, generator=gen) * 0.5
+    mod = kat.RatGroup(num_groups=G, numerator=a, denominator=b).to(dev)
+    xd = x.to(dev).requires_grad_(True)
+    y_ref = mod(xd)
+    y_ref.backward(gy.to(dev))
+    h_x, h_gy = x.pin_memory(), gy.pin_memory()
+    h_y = torch.empty_like(h_x).pin_memory()
+    h_dx = torch.empty_like(h_x).pin_memory()
+    h_grads = [torch.empty(6).pin_memory(), torch.empty(G, 4).pin_memory()]
+    ref_num = mod.weight_numerator.grad.clone()
+    mod.zero_grad(set_to_none=True)
+    pipe = HostPipeline(mod, chunks=6)
+    pipe.run(h_x, h_gy, h_y, h_dx, grads_host=h_grads)
+    torch.cuda.synchronize()
+    assert torch.equal(h_y, y_ref.detach().cpu())
+    assert torch.equal(h_dx, xd.grad.cpu())
+    torch.testing.assert_close(h_grads[0], ref_num.cpu(), rtol=1e-4, atol=1e-4)
+    _, _, da64, db64 = rat.rat_forward_backward(x.float().reshape(-1, 768), a, b,
+                                                gy.float().reshape(-1, 768),
+                                                compute_dtype=torch.float64)
+    _, _, nmag, dmag = rat.rat_magnitudes(x.float().reshape(-1, 768), a, b,
+                                          gy.float().reshape(-1, 768))
+    assert_coef_grads(h_grads[0], da64, nmag.sum(0), "pipeline rat d_num")
+    assert_coef_grads(h_grads[1], db64, dmag, "pipeline rat d_den")
