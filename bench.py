@@ -45,6 +45,14 @@ FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 
 
+def bwd_kernel_names() -> str:
+    """The kernels of one backward call for the streaming design in use."""
+    mode = os.environ.get("KAT_RATIONAL_PIPELINE", "async")
+    names = {"registers": "kat_bwd_kernel", "bulk": "kat_bwd_tma_kernel"}.get(
+        mode, "kat_bwd_async_kernel")
+    return names + " + kat_bwd_reduce_kernel (one C-ABI backward call)"
+
+
 def metric_for(workload) -> str:
     return "rat_cuda fwd+bwd Gelem/s" if workload.formula == 1 else METRIC
 
@@ -71,6 +79,8 @@ def parse_args():
                          "grkan_vit_b16)")
     ap.add_argument("--kat-exchange", choices=["ddp", "fused"], default="ddp",
                     help="how the ViT step exchanges the KAT coefficient gradients")
+    ap.add_argument("--vit-eager", action="store_true",
+                    help="eager ViT steps on one GPU instead of the captured CUDA graph")
     ap.add_argument("--vit-compare", action="store_true",
                     help="also time the ViT step with the reference's PyTorch KAT formulation "
                          "and with plain GELU MLPs (one GPU)")
@@ -414,9 +424,8 @@ def run_ours(args):
 
     fwd_ms = time_launches(fwd_fn, fwd_args, args.kernel_iters)
     bwd_ms = time_launches(bwd_fn, bwd_args, args.kernel_iters)
-    mode = os.environ.get("KAT_RATIONAL_PIPELINE", "async")
-    bwd_kernel_name = {"registers": "kat_bwd_kernel", "bulk": "kat_bwd_tma_kernel"}.get(
-        mode, "kat_bwd_async_kernel") + " + kat_bwd_reduce_kernel (one C-ABI backward call)"
+    bwd_kernel_name = bwd_kernel_names()
+    launches_per_step = 1 + bwd_kernel_name.count("+") + 1
     fwd_gbs = 2 * N * elem_bytes / (fwd_ms * 1e-3) / 1e9
     bwd_gbs = 3 * N * elem_bytes / (bwd_ms * 1e-3) / 1e9
 
@@ -520,7 +529,7 @@ def run_ours(args):
                     "api": f"rational_kat_cu_b200.host_io.HostPipeline ({args.e2e_chunks} "
                            f"row chunks, H2D / compute / D2H overlapped, consecutive steps "
                            f"overlapped)"},
-            "gpu_launches": 3 * args.steps * world,
+            "gpu_launches": launches_per_step * args.steps * world,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
@@ -770,20 +779,28 @@ def run_vit(args):
         return gv.GRKANViT(dataclasses.replace(cfg, act=act), kat_device=kat_device).to(
             dev, dtype=torch.bfloat16)
 
+    graphed = dist is None and not args.vit_eager
     model = build()
     net = model
     if dist is not None:
         net = gv.wrap_data_parallel(model, args.kat_exchange, device_ids=[local],
                                     timeout_ms=20000, gradient_as_bucket_view=True)
-    opt = gv.make_optimizer(model)
+    opt = gv.make_optimizer(model, capturable=graphed)
     h_img, h_lab = gv.synthetic_batch(B, cfg, dtype=torch.bfloat16, seed=rank, device=dev)
     d_img, d_lab = h_img.to(dev), h_lab.to(dev)
 
+    def make_step(m, o):
+        """One training step: the captured graph (one GPU) or an eager step."""
+        if graphed:
+            g = gv.GraphedTrainStep(m, o, d_img, d_lab)
+            return g, (lambda img=None, lab=None: g(img, lab))
+        return None, (lambda img=d_img, lab=d_lab: gv.train_step(m, o, img, lab))
+
+    graph_obj, step = make_step(net, opt)
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
-    ms = _time_steps(lambda: gv.train_step(net, opt, d_img, d_lab), args.steps, args.warmup,
-                     dev, stream, dist)
+    ms = _time_steps(lambda: step(), args.steps, args.warmup, dev, stream, dist)
     value = world * B / (ms * 1e-3)
 
     # End to end: every step uploads its images and labels from pinned host memory and
@@ -793,7 +810,7 @@ def run_vit(args):
     def e2e_step():
         img = h_img.to(dev, non_blocking=True)
         lab = h_lab.to(dev, non_blocking=True)
-        h_loss.copy_(gv.train_step(net, opt, img, lab), non_blocking=True)
+        h_loss.copy_(step(img, lab), non_blocking=True)
 
     e2e_ms = _time_steps(e2e_step, args.e2e_steps, 2, dev, stream, dist)
     loss_value = float(h_loss.item())
@@ -809,21 +826,25 @@ def run_vit(args):
     f2, b2, n2 = _kat_kernel_ms(dev, stream, (B, cfg.num_tokens, 4 * cfg.embed_dim), "gelu",
                                 cfg.num_groups, args.kernel_iters // 4 or 1)
     kat_ms = cfg.depth * (f1 + b1 + f2 + b2)
+    bwd2_names = bwd_kernel_names()
+    launches_per_step = cfg.depth * 2 * (1 + bwd2_names.count("+") + 1)
     peak, peak_kind = measured_peak()
     bwd_gbs = 3 * n2 * 2 / (b2 * 1e-3) / 1e9
 
     compare = None
     if args.vit_compare and world == 1:
         compare = {}
-        del opt
+        del opt, graph_obj, step
+        torch.cuda.empty_cache()
         for name, kw in (("kat_torch_formulation", dict(kat_device="cpu")),
                          ("gelu_mlp", dict(act="gelu"))):
             m2 = build(**kw)
-            o2 = gv.make_optimizer(m2)
+            o2 = gv.make_optimizer(m2, capturable=graphed)
+            g2, step2 = make_step(m2, o2)
             steps2 = max(5, min(args.steps, 30))
-            ms2 = _time_steps(lambda: gv.train_step(m2, o2, d_img, d_lab), steps2, 3, dev, stream)
+            ms2 = _time_steps(lambda: step2(), steps2, 3, dev, stream)
             compare[name] = {"ms_per_step": ms2, "images_s": B / (ms2 * 1e-3), "steps": steps2}
-            del m2, o2
+            del m2, o2, g2, step2
             torch.cuda.empty_cache()
         compare["kat_torch_formulation"]["what"] = (
             "KAT_Group on the reference's PyTorch formulation (power stack + bmm, "
@@ -852,12 +873,15 @@ def run_vit(args):
                 "seq_len": cfg.num_tokens, "parallelism": f"dp{world}",
                 "kat_exchange": args.kat_exchange if world > 1 else None,
                 "optimizer": "AdamW (fused)", "params": "bf16",
+                "step": ("forward + loss + backward + optimizer captured in one CUDA graph"
+                         if graphed else "eager" + (" with DistributedDataParallel over NCCL"
+                                                    if dist is not None else "")),
                 "l2": "activations of one step are far larger than L2 (no flush needed)",
                 "loss_last_step": loss_value,
             },
             "roofline": {
-                "bound": "hbm", "kernel": "KAT act2 backward call [B,197,3072] bf16 "
-                                          "(kat_bwd_async_kernel + kat_bwd_reduce_kernel)",
+                "bound": "hbm", "kernel": "KAT act2 backward call [B,197,3072] bf16: "
+                                          + bwd2_names,
                 "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
                 "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
                 "algorithmic_bytes_per_launch": 3 * n2 * 2, "ms_per_launch": b2,
@@ -873,7 +897,7 @@ def run_vit(args):
                     "d2h_bytes_per_step": world * 4, "ms_per_step": e2e_ms,
                     "api": "grkan_vit.train_step on pinned host images/labels (H2D per step), "
                            "loss read back to pinned host"},
-            "gpu_launches": 3 * 2 * cfg.depth * args.steps * world,
+            "gpu_launches": launches_per_step * args.steps * world,
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
@@ -886,9 +910,190 @@ def run_vit(args):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# B-spline basis (--workload bspline_kan): the fused Cox-de Boor basis of a KAN layer
+# ---------------------------------------------------------------------------
+
+BSPLINE_WORKLOAD = "bspline_kan"
+BSPLINE_METRIC = "B-spline basis fwd+bwd Gelem/s"
+BSPLINE_SHAPE = (16384, 1024, 8, 3)   # batch, in_features, grid_size, spline_order
+
+
+def _bspline_inputs(B, D, gs, order, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, D, generator=g) * 0.6
+    gb = torch.randn(B, D, gs + order, generator=g)
+    return x, gb
+
+
+def _bspline_grid(D, gs, order):
+    from rational_kat_cu_b200.bspline import FusedKANLinear
+
+    return FusedKANLinear(D, 1, grid_size=gs, spline_order=order).grid
+
+
+def _bspline_cpu_rate(budget_s: float, steps: int = 0, warmup: int = 0):
+    from oracle import bspline_oracle as bs
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    B, D, gs, order = BSPLINE_SHAPE
+    grid = _bspline_grid(D, gs, order)
+
+    def run(rows, n):
+        x, gb = _bspline_inputs(rows, D, gs, order)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            bs.b_splines_fwd_bwd(x, grid, order, gb)
+        return (time.perf_counter() - t0) / max(n, 1)
+
+    per_row = run(8, 1) / 8
+    n_calls = (steps + warmup) if steps else 3
+    rows = int(max(1, min(B, budget_s / max(n_calls, 1) / per_row)))
+    run(rows, warmup if steps else 1)
+    reps = steps if steps else 2
+    dt = run(rows, reps)
+    return rows * D / dt / 1e9, {
+        "cores": torch.get_num_threads(), "rows": rows, "seconds_per_step": dt, "reps": reps,
+        "sample": f"x[{rows},{D}], grid_size {gs}, order {order}: the reference's PyTorch "
+                  f"Cox-de Boor (oracle restatement) forward + autograd backward, fp32, mean of "
+                  f"{reps} timed steps"}
+
+
+def run_bspline_reference(args):
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    steps, warmup = min(args.steps, 5), min(args.warmup, 1)
+    rate, info = _bspline_cpu_rate(budget_s=min(150.0, 20.0 + 2.0 * (steps + warmup)),
+                                   steps=steps, warmup=warmup)
+    print(json.dumps({
+        "metric": BSPLINE_METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "warmup": warmup, "ms_per_step": info["seconds_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": BSPLINE_WORKLOAD, "shape": list(BSPLINE_SHAPE[:2]),
+                   "grid_size": BSPLINE_SHAPE[2], "spline_order": BSPLINE_SHAPE[3],
+                   "sample_rows": info["rows"]},
+        "cpu_baseline": {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_bspline(args):
+    """Step = basis forward + backward C-ABI launches on x [16384, 1024] fp32 (grid_size 8,
+    order 3: 11 basis values per element), inputs resident; e2e adds the host copies."""
+    import ctypes
+
+    from rational_kat_cu_b200 import _native
+
+    world, rank, local = dist_setup()
+    dist = init_process_group(world, rank, local) if world > 1 else None
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    B, D, gs, order = BSPLINE_SHAPE
+    nb = gs + order
+    nk = gs + 2 * order + 1
+    x_h, gb_h = _bspline_inputs(B, D, gs, order, seed=rank)
+    grid = _bspline_grid(D, gs, order).to(dev)
+    x, gb = x_h.to(dev), gb_h.to(dev)
+    bases = torch.empty(B, D, nb, device=dev)
+    dx = torch.empty(B, D, device=dev)
+    lib = _native.lib()
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    fa = (x.data_ptr(), grid.data_ptr(), bases.data_ptr(), B, D, nk, order, sp)
+    ba = (x.data_ptr(), grid.data_ptr(), gb.data_ptr(), dx.data_ptr(), B, D, nk, order, sp)
+
+    def step():
+        _native.check("fwd", lib.kat_bspline_basis_fwd(*fa))
+        _native.check("bwd", lib.kat_bspline_basis_bwd(*ba))
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = _time_steps(step, args.steps, args.warmup, dev, stream, dist)
+    iters = args.kernel_iters
+
+    def per_launch(fn, a):
+        for _ in range(3):
+            fn(*a)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn(*a)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / iters
+
+    f_ms = per_launch(lib.kat_bspline_basis_fwd, fa)
+    b_ms = per_launch(lib.kat_bspline_basis_bwd, ba)
+    # e2e: pinned host x and grad_bases in, bases and dx back, every step
+    hx, hgb = x_h.pin_memory(), gb_h.pin_memory()
+    hb = torch.empty(B, D, nb, pin_memory=True)
+    hdx = torch.empty(B, D, pin_memory=True)
+
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        gb.copy_(hgb, non_blocking=True)
+        step()
+        hb.copy_(bases, non_blocking=True)
+        hdx.copy_(dx, non_blocking=True)
+
+    e_ms = _time_steps(e2e_step, max(2, args.e2e_steps // 2), 1, dev, stream, dist)
+    clocks = None
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        rate, info = _bspline_cpu_rate(budget_s=args.cpu_seconds)
+        cpu = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
+               "sample": info["sample"]}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        N = B * D
+        peak, peak_kind = measured_peak()
+        fwd_bytes, bwd_bytes = N * 4 * (1 + nb), N * 4 * (2 + nb)
+        print(json.dumps({
+            "metric": BSPLINE_METRIC, "value": world * N / (ms * 1e-3) / 1e9, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": BSPLINE_WORKLOAD, "shape": [B, D], "grid_size": gs,
+                       "spline_order": order, "n_basis": nb,
+                       "l2": f"bases {N * nb * 4 / 1e6:.0f} MB per step, larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "kat_bspline_fwd_kernel<3>",
+                         "achieved": fwd_bytes / (f_ms * 1e-3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": fwd_bytes / (f_ms * 1e-3) / 1e9 / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                         "algorithmic_bytes_per_launch": fwd_bytes, "ms_per_launch": f_ms},
+            "kernels": {"fwd_ms": f_ms, "bwd_ms": b_ms,
+                        "fwd_frac": fwd_bytes / (f_ms * 1e-3) / 1e9 / peak,
+                        "bwd_frac": bwd_bytes / (b_ms * 1e-3) / 1e9 / peak,
+                        "step_hbm_frac": (fwd_bytes + bwd_bytes) / (ms * 1e-3) / 1e9 / peak},
+            "e2e": {"value": world * N / (e_ms * 1e-3) / 1e9, "unit": UNIT,
+                    "h2d_bytes_per_step": world * N * 4 * (1 + nb),
+                    "d2h_bytes_per_step": world * N * 4 * (1 + nb), "ms_per_step": e_ms,
+                    "api": "C ABI kat_bspline_basis_fwd/_bwd with pinned host copies"},
+            "gpu_launches": 2 * args.steps * world,
+            "cpu_baseline": cpu, "clocks": clocks,
+        }), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.workload == VIT_WORKLOAD:
+    if args.workload == BSPLINE_WORKLOAD:
+        if args.impl == "reference":
+            run_bspline_reference(args)
+        else:
+            run_bspline(args)
+    elif args.workload == VIT_WORKLOAD:
         if args.impl == "reference":
             run_vit_reference(args)
         else:

@@ -4,9 +4,11 @@ Public API, matching the reference package `kat_rational` (kat_rational/__init__
 KAT_Group, KAT_Group2D, KAT_Group_Torch and the autograd Functions (also under their
 reference names RationalTriton1DGroup / RationalTriton2D); and the reference package
 `rational_kat_cu`'s front end rat_cuda (rational_kat_cu/__init__.py), the abs-after-sum
-variant of the activation on the same kernels.
+variant of the activation on the same kernels; and its B-spline basis kernels with the
+FusedKANLinear layer (rational_kat_cu/bspline_basis.py).
 """
 
+from .bspline import BSplineBasis, FusedKANLinear, bspline_basis_bwd, bspline_basis_fwd
 from .kat_1dgroup import KAT_Group
 from .kat_1dgroup_torch import KAT_Group_Torch, Rational_CUDA_A_1DGroup
 from .kat_2dgroup import KAT_Group2D
@@ -37,4 +39,8 @@ __all__ = [
     "rational_bwd_cuda_2d",
     "rat_cuda",
     "RatGroup",
+    "BSplineBasis",
+    "FusedKANLinear",
+    "bspline_basis_fwd",
+    "bspline_basis_bwd",
 ]

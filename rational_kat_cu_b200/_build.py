@@ -1,8 +1,9 @@
 """Build recipe for libkat_rational.so (the sm_100a kernels behind the C ABI).
 
-`build()` runs nvcc on csrc/kat_rational.cu for `-gencode arch=compute_100a,code=sm_100a`
-and writes the shared library next to this file, so it travels with the source tree.
-It rebuilds only when the source or the public header is newer than the library.
+`build()` runs nvcc on csrc/kat_rational.cu and csrc/kat_bspline.cu for
+`-gencode arch=compute_100a,code=sm_100a` and writes the shared library next to this file, so
+it travels with the source tree.  It rebuilds only when a source or a public header is newer
+than the library.
 """
 
 from __future__ import annotations
@@ -14,8 +15,10 @@ import sys
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
-SOURCE = os.path.join(PKG_DIR, "csrc", "kat_rational.cu")
-HEADER = os.path.join(REPO_DIR, "include", "kat_rational.h")
+SOURCES = [os.path.join(PKG_DIR, "csrc", "kat_rational.cu"),
+           os.path.join(PKG_DIR, "csrc", "kat_bspline.cu")]
+HEADERS = [os.path.join(REPO_DIR, "include", "kat_rational.h"),
+           os.path.join(REPO_DIR, "include", "kat_bspline.h")]
 LIBRARY = os.path.join(PKG_DIR, "libkat_rational.so")
 
 NVCC_FLAGS = [
@@ -38,7 +41,7 @@ def is_stale() -> bool:
     if not os.path.exists(LIBRARY):
         return True
     lib_t = os.path.getmtime(LIBRARY)
-    return any(os.path.getmtime(p) > lib_t for p in (SOURCE, HEADER, __file__))
+    return any(os.path.getmtime(p) > lib_t for p in (*SOURCES, *HEADERS, __file__))
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -46,7 +49,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not is_stale():
         return LIBRARY
     cmd = [find_nvcc(), *NVCC_FLAGS, "-I", os.path.join(REPO_DIR, "include"),
-           "-o", LIBRARY + ".tmp", SOURCE]
+           "-o", LIBRARY + ".tmp", *SOURCES]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)

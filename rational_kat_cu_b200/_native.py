@@ -1,4 +1,5 @@
-"""ctypes binding of libkat_rational.so (the C ABI declared in include/kat_rational.h).
+"""ctypes binding of libkat_rational.so (the C ABI declared in include/kat_rational.h and
+include/kat_bspline.h).
 
 The library is loaded once, on first use.  If it is missing the call fails with a
 RuntimeError naming the build command: there is no fallback implementation.
@@ -29,8 +30,10 @@ KAT_ERR_BAD_FORMULA = 8
 KAT_FORMULA_KAT = 0
 KAT_FORMULA_ABS_SUM = 1
 
-# Every symbol include/kat_rational.h declares.
+# Every symbol include/*.h declares.
 EXPORTED_SYMBOLS = (
+    "kat_bspline_basis_fwd",
+    "kat_bspline_basis_bwd",
     "kat_rational_fwd",
     "kat_rational_bwd",
     "kat_rational_fwd_formula",
@@ -125,6 +128,12 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_bwd_formula.restype = i32
     lib.kat_rational_fwd_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
     lib.kat_rational_fwd_f64.restype = i32
+    lib.kat_bspline_basis_fwd.argtypes = [vp, vp, vp, i64, i64, ctypes.c_int32, ctypes.c_int32,
+                                          vp]
+    lib.kat_bspline_basis_fwd.restype = i32
+    lib.kat_bspline_basis_bwd.argtypes = [vp, vp, vp, vp, i64, i64, ctypes.c_int32,
+                                          ctypes.c_int32, vp]
+    lib.kat_bspline_basis_bwd.restype = i32
     lib.kat_rational_bwd_workspace_size.argtypes = [i64, i64, i64, i64, i32, i32,
                                                     ctypes.POINTER(ctypes.c_size_t)]
     lib.kat_rational_bwd_workspace_size.restype = i32

@@ -105,7 +105,8 @@ class Attention(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         B, L, C = x.shape
         qkv = self.qkv(x).view(B, L, 3, self.num_heads, C // self.num_heads).permute(2, 0, 3, 1, 4)
-        o = F.scaled_dot_product_attention(qkv[0], qkv[1], qkv[2])
+        q, k, v = qkv.unbind(0)   # (indexing would make its backward zero-fill the whole qkv)
+        o = F.scaled_dot_product_attention(q, k, v)
         return self.proj(o.transpose(1, 2).reshape(B, L, C))
 
 
@@ -198,11 +199,14 @@ def wrap_data_parallel(model: nn.Module, kat_exchange: str = "ddp", device_ids=N
     return DDP(model, device_ids=device_ids, **ddp_kwargs)
 
 
-def make_optimizer(model: nn.Module, lr: float = 1e-4, weight_decay: float = 0.05):
-    """AdamW; the fused CUDA implementation when the parameters are on a GPU."""
+def make_optimizer(model: nn.Module, lr: float = 1e-4, weight_decay: float = 0.05,
+                   capturable: bool = False):
+    """AdamW; the fused CUDA implementation when the parameters are on a GPU (capturable=True
+    for use inside a CUDA graph)."""
     params = list(model.parameters())
     fused = bool(params) and params[0].is_cuda
-    return torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, fused=fused)
+    return torch.optim.AdamW(params, lr=lr, weight_decay=weight_decay, fused=fused,
+                             capturable=capturable and fused)
 
 
 def train_step(model: nn.Module, optimizer, images: torch.Tensor,
@@ -215,6 +219,43 @@ def train_step(model: nn.Module, optimizer, images: torch.Tensor,
     loss.backward()
     optimizer.step()
     return loss.detach()
+
+
+class GraphedTrainStep:
+    """The whole training step — forward, loss, backward and the optimizer update — captured
+    once in a CUDA graph and replayed, so a step costs its kernels and not the ~800 Python-side
+    launches of an eager step.  Inputs are copied into static device buffers before each replay.
+    The optimizer must be capturable (make_optimizer(capturable=True)).  One process per GPU,
+    no DistributedDataParallel inside (the fused KAT coefficient exchange may be inside)."""
+
+    def __init__(self, model: nn.Module, optimizer, images: torch.Tensor, labels: torch.Tensor,
+                 warmup: int = 3):
+        self.model, self.optimizer = model, optimizer
+        self.images = images.detach().clone()
+        self.labels = labels.detach().clone()
+        side = torch.cuda.Stream(self.images.device)
+        side.wait_stream(torch.cuda.current_stream(self.images.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                train_step(model, optimizer, self.images, self.labels)
+        torch.cuda.current_stream(self.images.device).wait_stream(side)
+        optimizer.zero_grad(set_to_none=True)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            logits = model(self.images)
+            self.loss = F.cross_entropy(logits.float(), self.labels)
+            self.loss.backward()
+            optimizer.step()
+
+    def __call__(self, images: torch.Tensor = None, labels: torch.Tensor = None) -> torch.Tensor:
+        """Replay one step (after copying new inputs in, if given); returns the loss tensor
+        (device, overwritten by the next replay)."""
+        if images is not None:
+            self.images.copy_(images, non_blocking=True)
+        if labels is not None:
+            self.labels.copy_(labels, non_blocking=True)
+        self.graph.replay()
+        return self.loss
 
 
 def synthetic_batch(batch: int, cfg: ViTConfig, dtype=torch.bfloat16, seed: int = 0,

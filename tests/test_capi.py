@@ -1,5 +1,4 @@
-"""The C ABI library on the CPU: it loads, exports every symbol include/kat_rational.h
-declares, rejects bad arguments before touching a GPU, and its launch geometry covers every
+"""The C ABI library on the CPU: it loads, exports every symbol include/*.h declares, rejects bad arguments before touching a GPU, and its launch geometry covers every
 element exactly once with a consistent partial-sum layout (checked by a host-side
 restatement of the kernels' index arithmetic)."""
 
@@ -11,14 +10,16 @@ import pytest
 
 from rational_kat_cu_b200 import _native
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
-                      "kat_rational.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(kat_rational_\w+)\s*\(", text)))
+    names = set()
+    for h in sorted(os.listdir(INCLUDE)):
+        if h.endswith(".h"):
+            text = re.sub(r"/\*.*?\*/", "", open(os.path.join(INCLUDE, h)).read(), flags=re.S)
+            names |= set(re.findall(r"\b(kat_\w+)\s*\(", text))
+    return sorted(names)
 
 
 def test_header_declares_expected_entry_points():
@@ -38,6 +39,20 @@ def test_strerror_covers_every_status():
     assert texts[0] == "success"
     assert len(set(texts.values())) == 7
     assert "unknown" in _native.strerror(99)
+
+
+def test_bspline_entry_points_validate_before_launch():
+    lib = _native.lib()
+    E = _native
+    for nk, order in ((15, 0), (15, 6), (4, 3), (65, 3)):
+        assert lib.kat_bspline_basis_fwd(1, 1, 1, 4, 8, nk, order, None) == E.KAT_ERR_BAD_SHAPE
+        assert lib.kat_bspline_basis_bwd(1, 1, 1, 1, 4, 8, nk, order, None) == E.KAT_ERR_BAD_SHAPE
+    assert lib.kat_bspline_basis_fwd(1, 1, 1, -1, 8, 15, 3, None) == E.KAT_ERR_BAD_SHAPE
+    assert lib.kat_bspline_basis_fwd(None, 1, 1, 4, 8, 15, 3, None) == E.KAT_ERR_NULL_POINTER
+    assert lib.kat_bspline_basis_bwd(1, 1, None, 1, 4, 8, 15, 3, None) == E.KAT_ERR_NULL_POINTER
+    # empty problems are a successful no-op
+    assert lib.kat_bspline_basis_fwd(None, None, None, 0, 8, 15, 3, None) == E.KAT_OK
+    assert lib.kat_bspline_basis_bwd(None, None, None, None, 4, 0, 15, 3, None) == E.KAT_OK
 
 
 def test_formula_entry_points_validate_before_launch():

@@ -111,6 +111,29 @@ def test_vit_bf16_training_decreases_loss(cuda_device):
         assert torch.isfinite(m.weight_denominator).all()
 
 
+def test_graphed_train_step_tracks_eager(cuda_device):
+    """The CUDA-graph step (forward, backward, fused AdamW replayed) follows the eager step's
+    loss trajectory on the same model, data and optimizer settings."""
+    cfg = small_cfg()
+    images, labels = gv.synthetic_batch(16, cfg, dtype=torch.bfloat16, seed=11)
+    images, labels = images.to(cuda_device), labels.to(cuda_device)
+    losses = {}
+    for mode in ("eager", "graph"):
+        torch.manual_seed(0)
+        model = gv.GRKANViT(cfg).to(cuda_device, dtype=torch.bfloat16)
+        opt = gv.make_optimizer(model, lr=1e-3, capturable=(mode == "graph"))
+        if mode == "graph":
+            # the three warm-up steps before capture are ordinary training steps
+            step = gv.GraphedTrainStep(model, opt, images, labels, warmup=3)
+            losses[mode] = [step().item() for _ in range(8)]
+        else:
+            all_losses = [gv.train_step(model, opt, images, labels).item() for _ in range(11)]
+            losses[mode] = all_losses[3:]
+    torch.testing.assert_close(torch.tensor(losses["graph"]), torch.tensor(losses["eager"]),
+                               rtol=2e-2, atol=2e-2)
+    assert losses["graph"][-1] < losses["graph"][0]
+
+
 WORKER = r'''
 import os, sys, datetime
 sys.path.insert(0, {repo!r})

@@ -49,3 +49,4 @@ def test_pipeline_mode_parity(mode):
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                          timeout=600)
     assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stdout + res.stderr
+
