@@ -1,22 +1,33 @@
 // B-spline basis (Cox-de Boor) forward and backward for sm_100a: the basis evaluation of
 // efficient-KAN layers that the reference fuses in rational_kat_cu/bspline_basis.py.
 //
-// One thread per input element x[b, d].  Instead of running the recursion over every knot
-// interval (the reference evaluates all n_knots - 1 indicators and every level in full), a
-// thread finds the one interval t_i <= x < t_{i+1} by binary search on its channel's knots and
-// evaluates only the triangle of values that can be non-zero there (k + 1 values at level k),
-// each term with the reference's operation order — ((x - t_j) / max(t_{j+k} - t_j, 1e-8)) times
-// the lower-order value, the two terms added, no fused multiply-add — so the non-zero values
-// match the full recursion bit for bit and every other basis value is zero, as there.
-// Outputs (forward) and incoming gradients (backward) move through shared memory so each
-// block reads and writes its contiguous [elements x n_basis] slab with coalesced accesses.
+// Work split: a block of 256 threads takes tiles of 8 batch rows x 32 features (warp w = row w,
+// lane = feature), walking the tiles of one 32-feature column before the next, so it keeps
+// those 32 features' knots in shared memory together with the correctly rounded reciprocals
+// of every knot difference the recursion divides by (1 / max(t_{j+k} - t_j, 1e-8), per
+// feature, level k and index j).
 //
-// Knots must be non-decreasing along each channel (KANLinear's grid and update_grid produce
+// Per element, instead of running the recursion over every knot interval (the reference
+// evaluates all n_knots - 1 indicators and every level in full), a thread finds the one
+// interval t_i <= x < t_{i+1} by binary search and evaluates only the triangle of values that
+// can be non-zero there (k + 1 values at level k), each term in the reference's operation order
+// — ((x - t_j) / max(t_{j+k} - t_j, 1e-8)) times the lower-order value, the two terms added, no
+// fused multiply-add between them — so the non-zero values match the full recursion bit for
+// bit and every other basis value is zero, as there.  Each division a / b is evaluated as
+// Markstein's FMA-corrected product with the tabulated reciprocal y = RN(1/b):
+// q0 = RN(a y), r = a - b q0 (exact, one FMA), q = RN(q0 + r y), which is the correctly
+// rounded quotient RN(a / b) (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) — the IEEE division result at
+// three FP32 operations.  Outputs (forward) and incoming gradients (backward) go through
+// shared memory so each row of a tile moves as one contiguous, coalesced range.
+//
+// Knots must be non-decreasing along each feature (KANLinear's grid and update_grid produce
 // such grids).  A non-finite x gives NaN in every basis value, as the reference's full
 // recursion does (its 0 * inf terms).
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 
@@ -25,39 +36,94 @@
 
 namespace {
 
-constexpr int kBsThreads = 256;
+constexpr int kTileCols = 32;   // features per tile (one warp)
+constexpr int kTileRows = 8;    // batch rows per tile (one per warp)
+constexpr int kBsThreads = kTileCols * kTileRows;
 constexpr int kMaxOrder = 5;
 constexpr int kMaxKnots = 64;
 constexpr float kEps = 1e-8f;
 
-// Largest i in [0, n - 2] with t[i] <= x, for t[0] <= x < t[n - 1] (non-decreasing t).
-__device__ __forceinline__ int find_span(const float* __restrict__ t, int n, float x) {
-  int lo = 0, hi = n - 1;  // invariant: t[lo] <= x < t[hi]
+// RN(a / b) from y = RN(1 / b) (Markstein's correction step).
+__device__ __forceinline__ float div_by(float a, float b, float y) {
+  const float q0 = __fmul_rn(a, y);
+  const float r = __fmaf_rn(-q0, b, a);
+  return __fmaf_rn(r, y, q0);
+}
+
+// Shared-memory layout of one column of tiles.
+// Knots and reciprocals are stored feature-minor ([index][32 features]): lane c reads
+// word index * 32 + c, in its own bank whatever index it needs, so the data-dependent span
+// lookups never conflict.
+struct Smem {
+  float* knots;   // [n_knots][32]
+  float* recip;   // [kOrder][n_knots][32]: 1 / max(t_{j+k} - t_j, eps) at [k - 1][j][c]
+  float* slab;    // [8][32 * n_basis]
+};
+
+size_t smem_bytes(int n_knots, int order) {
+  const int nb = n_knots - 1 - order;
+  return sizeof(float) * (size_t(kTileCols) * n_knots + size_t(kTileCols) * order * n_knots +
+                          size_t(kTileRows) * kTileCols * nb);
+}
+
+// Load the knots of features c0 .. c0 + 31 and tabulate the reciprocals.
+template <int kOrder>
+__device__ __forceinline__ void load_column(const Smem& sm, const float* __restrict__ grid,
+                                            int64_t features, int n_knots, int64_t c0) {
+  const int ncols = int(min(int64_t(kTileCols), features - c0));
+  for (int q = threadIdx.x; q < kTileCols * n_knots; q += kBsThreads) {
+    const int c = q % kTileCols, j = q / kTileCols;
+    sm.knots[q] = c < ncols ? grid[(c0 + c) * n_knots + j] : 0.0f;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < kTileCols * kOrder * n_knots; q += kBsThreads) {
+    const int c = q % kTileCols, kj = q / kTileCols;
+    const int k = kj / n_knots + 1, j = kj - (k - 1) * n_knots;
+    float v = 0.0f;
+    if (j + k < n_knots)
+      v = __frcp_rn(fmaxf(__fsub_rn(sm.knots[(j + k) * kTileCols + c],
+                                    sm.knots[j * kTileCols + c]), kEps));
+    sm.recip[q] = v;
+  }
+  __syncthreads();
+}
+
+// Largest i in [0, n - 2] with t_i <= x, for t_0 <= x < t_{n-1} (non-decreasing t); knot t_j
+// of this lane's feature is t[j * 32].
+__device__ __forceinline__ int find_span(const float* t, int n, float x) {
+  int lo = 0, hi = n - 1;  // invariant: t_lo <= x < t_hi
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (__ldg(t + mid) <= x) lo = mid; else hi = mid;
+    if (t[mid * kTileCols] <= x) lo = mid; else hi = mid;
   }
   return lo;
 }
 
-// Knots t[i - kOrder .. i + kOrder + 1] of span i in registers (indices outside [0, n - 1] are
-// clamped: those entries are never used, see span_basis).
+// The knots t[i - kOrder .. i + kOrder + 1] of span i (w[q] = t[i - kOrder + q]) and, per level
+// k, the reciprocals 1 / max(t_{j+k} - t_j, eps) for j = i - k + 1 .. i (rw[k - 1][m - 1], m =
+// 1..k): everything the triangle reads, moved from shared memory to registers once.  Indices
+// outside the knot vector are clamped; those values are never used (see span_basis).
 template <int kOrder>
-__device__ __forceinline__ void load_window(const float* __restrict__ t, int n, int i,
-                                            float (&w)[2 * kOrder + 2]) {
+__device__ __forceinline__ void load_span(const float* t, const float* rc, int n, int i,
+                                          float (&w)[2 * kOrder + 2],
+                                          float (&rw)[kOrder][kOrder]) {
 #pragma unroll
-  for (int q = 0; q < 2 * kOrder + 2; ++q) {
-    const int j = min(max(i - kOrder + q, 0), n - 1);
-    w[q] = __ldg(t + j);
+  for (int q = 0; q < 2 * kOrder + 2; ++q)
+    w[q] = t[min(max(i - kOrder + q, 0), n - 1) * kTileCols];
+#pragma unroll
+  for (int k = 1; k <= kOrder; ++k) {
+#pragma unroll
+    for (int m = 1; m <= k; ++m)
+      rw[k - 1][m - 1] = rc[((k - 1) * n + max(i - k + m, 0)) * kTileCols];
   }
 }
 
 // Basis values of order kOrder that can be non-zero at x in span i: b[m] = B^kOrder_{i-kOrder+m}
-// for m = 0..kOrder (entries whose index is outside [0, n - 2 - kOrder] are left 0), and,
-// when kGrad, their derivatives db[m].  Level by level, as the recursion runs; knot t_j is
-// w[j - i + kOrder].
+// for m = 0..kOrder (entries whose index is outside [0, n - 2 - kOrder] are left 0), and, when
+// kGrad, their derivatives db[m].  Knot t_j is w[j - i + kOrder].
 template <int kOrder, bool kGrad>
-__device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2], int n, int i,
+__device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2],
+                                           const float (&rw)[kOrder][kOrder], int n, int i,
                                            float x, float (&b)[kMaxOrder + 1],
                                            float (&db)[kMaxOrder + 1]) {
   float prev[kMaxOrder + 1], dprev[kMaxOrder + 1];
@@ -75,19 +141,21 @@ __device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2], int
         float left = 0.0f, dleft = 0.0f;
         if (m >= 1) {
           const float d1 = fmaxf(__fsub_rn(w[o + k], w[o]), kEps);
-          const float u = __fdiv_rn(__fsub_rn(x, w[o]), d1);
+          const float y1 = rw[k - 1][m - 1];
+          const float u = div_by(__fsub_rn(x, w[o]), d1, y1);
           left = __fmul_rn(u, prev[m - 1]);
           if constexpr (kGrad)
-            dleft = __fadd_rn(__fdiv_rn(prev[m - 1], d1), __fmul_rn(u, dprev[m - 1]));
+            dleft = __fadd_rn(div_by(prev[m - 1], d1, y1), __fmul_rn(u, dprev[m - 1]));
         }
         // right term: (t_{j+k+1} - x) / max(t_{j+k+1} - t_{j+1}, eps) * B^{k-1}_{j+1}   (m)
         float right = 0.0f, dright = 0.0f;
         if (m <= k - 1) {
           const float d2 = fmaxf(__fsub_rn(w[o + k + 1], w[o + 1]), kEps);
-          const float r = __fdiv_rn(__fsub_rn(w[o + k + 1], x), d2);
+          const float y2 = rw[k - 1][m];
+          const float r = div_by(__fsub_rn(w[o + k + 1], x), d2, y2);
           right = __fmul_rn(r, prev[m]);
           if constexpr (kGrad)
-            dright = __fsub_rn(__fmul_rn(r, dprev[m]), __fdiv_rn(prev[m], d2));
+            dright = __fsub_rn(__fmul_rn(r, dprev[m]), div_by(prev[m], d2, y2));
         }
         v = __fadd_rn(left, right);
         if constexpr (kGrad) dv = __fadd_rn(dleft, dright);
@@ -103,112 +171,145 @@ __device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2], int
   }
 }
 
-// Channel of element e0 + threadIdx.x, given d0 = e0 % features (one division per block).
-__device__ __forceinline__ int64_t channel_of(int64_t d0, int64_t features) {
-  int64_t d = d0 + threadIdx.x;
-  if (features >= blockDim.x) return d >= features ? d - features : d;
-  return d % features;
-}
-
-// Copies `count` floats between global memory and the block's slab with 16-byte accesses
-// when both sides are 16-byte aligned (the slab always is; the global side is when the
-// block's first float is), scalar otherwise.
+// Warp-wide copy of `count` floats between a tile row's slab (16-byte aligned) and global
+// memory: 16-byte accesses when the global side is 16-byte aligned, else 4-byte ones.
 template <bool kToGlobal>
-__device__ __forceinline__ void copy_slab(float* __restrict__ slab, float* __restrict__ g,
-                                          int count) {
+__device__ __forceinline__ void warp_copy(float* __restrict__ slab, float* __restrict__ g,
+                                          int count, int lane) {
   if ((reinterpret_cast<uintptr_t>(g) & 15) == 0) {
     const int c4 = count >> 2;
     float4* s4 = reinterpret_cast<float4*>(slab);
     float4* g4 = reinterpret_cast<float4*>(g);
-#pragma unroll 4
-    for (int q = threadIdx.x; q < c4; q += kBsThreads) {
+    for (int q = lane; q < c4; q += 32) {
       if constexpr (kToGlobal) g4[q] = s4[q]; else s4[q] = __ldg(g4 + q);
     }
-    for (int q = (c4 << 2) + threadIdx.x; q < count; q += kBsThreads) {
+    for (int q = (c4 << 2) + lane; q < count; q += 32) {
       if constexpr (kToGlobal) g[q] = slab[q]; else slab[q] = __ldg(g + q);
     }
   } else {
-#pragma unroll 4
-    for (int q = threadIdx.x; q < count; q += kBsThreads) {
+    for (int q = lane; q < count; q += 32) {
       if constexpr (kToGlobal) g[q] = slab[q]; else slab[q] = __ldg(g + q);
     }
   }
+}
+
+// Contiguous range of one tile row: features c0 .. c0 + ncols - 1 of batch row `row`.
+__device__ __forceinline__ int64_t row_offset(int64_t row, int64_t features, int64_t c0, int nb) {
+  return (row * features + c0) * nb;
+}
+
+// Tiles are numbered column-major (all row tiles of feature column 0, then column 1, ...);
+// block b takes the contiguous tile range [b * q + min(b, r), ...).
+__device__ __forceinline__ void block_tiles(int64_t n_tiles, int64_t& t0, int64_t& t1) {
+  const int64_t q = n_tiles / gridDim.x, r = n_tiles % gridDim.x, b = blockIdx.x;
+  t0 = b * q + min(b, r);
+  t1 = t0 + q + (b < r ? 1 : 0);
 }
 
 template <int kOrder>
 __global__ void __launch_bounds__(kBsThreads)
 kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ grid,
-                       float* __restrict__ out, int64_t n_elem, int64_t features, int n_knots) {
-  extern __shared__ __align__(16) float slab[];  // [kBsThreads][n_basis]
-  __shared__ int64_t s_d0;
+                       float* __restrict__ out, int64_t batch, int64_t features, int n_knots) {
+  extern __shared__ __align__(16) float smem[];
   const int nb = n_knots - 1 - kOrder;
-  const int64_t e0 = int64_t(blockIdx.x) * kBsThreads;
-  const int count = int(min(int64_t(kBsThreads), n_elem - e0)) * nb;
-  if (threadIdx.x == 0) s_d0 = e0 % features;
-  {
-    float4* s4 = reinterpret_cast<float4*>(slab);
-    const int c4 = (kBsThreads * nb + 3) >> 2;
-    for (int q = threadIdx.x; q < c4; q += kBsThreads) s4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  __syncthreads();
-  const int64_t e = e0 + threadIdx.x;
-  if (e < n_elem) {
-    const float v = x[e];
-    const float* t = grid + channel_of(s_d0, features) * n_knots;
-    float* row = slab + threadIdx.x * nb;
-    if (!isfinite(v)) {
-      for (int j = 0; j < nb; ++j) row[j] = __int_as_float(0x7fc00000);
-    } else if (v >= __ldg(t) && v < __ldg(t + n_knots - 1)) {
-      const int i = find_span(t, n_knots, v);
-      float w[2 * kOrder + 2];
-      load_window<kOrder>(t, n_knots, i, w);
-      float b[kMaxOrder + 1], db[kMaxOrder + 1];
-      span_basis<kOrder, false>(w, n_knots, i, v, b, db);
+  const Smem sm{smem, smem + kTileCols * n_knots, smem + kTileCols * n_knots * (1 + kOrder)};
+  const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
+  const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
+  int64_t t0, t1;
+  block_tiles(row_tiles * col_tiles, t0, t1);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int64_t loaded = -1;
+  for (int64_t tile = t0; tile < t1; ++tile) {
+    const int64_t ct = tile / row_tiles, rt = tile - ct * row_tiles;
+    const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
+    const int ncols = int(min(int64_t(kTileCols), features - c0));
+    if (ct != loaded) {
+      __syncthreads();   // the previous column's tables are no longer read
+      load_column<kOrder>(sm, grid, features, n_knots, c0);
+      loaded = ct;
+    }
+    float* srow = sm.slab + w * (kTileCols * nb);
+    {
+      float4* s4 = reinterpret_cast<float4*>(srow);   // 32 * nb floats: a multiple of 4
+      for (int q = lane; q < (kTileCols * nb) >> 2; q += 32) s4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncwarp();
+    if (row < batch && lane < ncols) {
+      const float v = x[row * features + c0 + lane];
+      const float* t = sm.knots + lane;
+      float* r = srow + lane * nb;
+      if (!isfinite(v)) {
+        for (int j = 0; j < nb; ++j) r[j] = __int_as_float(0x7fc00000);
+      } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
+        const int i = find_span(t, n_knots, v);
+        float w[2 * kOrder + 2], rw[kOrder][kOrder];
+        load_span<kOrder>(t, sm.recip + lane, n_knots, i, w, rw);
+        float b[kMaxOrder + 1], db[kMaxOrder + 1];
+        span_basis<kOrder, false>(w, rw, n_knots, i, v, b, db);
 #pragma unroll
-      for (int m = 0; m <= kOrder; ++m) {
-        const int j = i - kOrder + m;
-        if (j >= 0 && j < nb) row[j] = b[m];
+        for (int m = 0; m <= kOrder; ++m) {
+          const int j = i - kOrder + m;
+          if (j >= 0 && j < nb) r[j] = b[m];
+        }
       }
     }
+    __syncwarp();
+    if (row < batch) warp_copy<true>(srow, out + row_offset(row, features, c0, nb), ncols * nb, lane);
+    __syncwarp();
   }
-  __syncthreads();
-  copy_slab<true>(slab, out + e0 * nb, count);
 }
 
 template <int kOrder>
 __global__ void __launch_bounds__(kBsThreads)
 kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ grid,
-                       const float* __restrict__ gb, float* __restrict__ gx, int64_t n_elem,
+                       const float* __restrict__ gb, float* __restrict__ gx, int64_t batch,
                        int64_t features, int n_knots) {
-  extern __shared__ __align__(16) float slab[];  // [kBsThreads][n_basis]
-  __shared__ int64_t s_d0;
+  extern __shared__ __align__(16) float smem[];
   const int nb = n_knots - 1 - kOrder;
-  const int64_t e0 = int64_t(blockIdx.x) * kBsThreads;
-  const int count = int(min(int64_t(kBsThreads), n_elem - e0)) * nb;
-  if (threadIdx.x == 0) s_d0 = e0 % features;
-  copy_slab<false>(slab, const_cast<float*>(gb) + e0 * nb, count);
-  __syncthreads();
-  const int64_t e = e0 + threadIdx.x;
-  if (e >= n_elem) return;
-  const float v = x[e];
-  const float* row = slab + threadIdx.x * nb;
-  float acc = 0.0f;
-  const float* t = grid + channel_of(s_d0, features) * n_knots;
-  if (!isfinite(v)) {
-    acc = __int_as_float(0x7fc00000);
-  } else if (v >= __ldg(t) && v < __ldg(t + n_knots - 1)) {
-    const int i = find_span(t, n_knots, v);
-    float w[2 * kOrder + 2];
-    load_window<kOrder>(t, n_knots, i, w);
-    float b[kMaxOrder + 1], db[kMaxOrder + 1];
-    span_basis<kOrder, true>(w, n_knots, i, v, b, db);
-#pragma unroll
-    for (int m = 0; m <= kOrder; ++m) {
-      const int j = i - kOrder + m;
-      if (j >= 0 && j < nb) acc = __fadd_rn(acc, __fmul_rn(row[j], db[m]));
+  const Smem sm{smem, smem + kTileCols * n_knots, smem + kTileCols * n_knots * (1 + kOrder)};
+  const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
+  const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
+  int64_t t0, t1;
+  block_tiles(row_tiles * col_tiles, t0, t1);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int64_t loaded = -1;
+  for (int64_t tile = t0; tile < t1; ++tile) {
+    const int64_t ct = tile / row_tiles, rt = tile - ct * row_tiles;
+    const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
+    const int ncols = int(min(int64_t(kTileCols), features - c0));
+    if (ct != loaded) {
+      __syncthreads();
+      load_column<kOrder>(sm, grid, features, n_knots, c0);
+      loaded = ct;
     }
+    float* srow = sm.slab + w * (kTileCols * nb);
+    if (row < batch)
+      warp_copy<false>(srow, const_cast<float*>(gb) + row_offset(row, features, c0, nb), ncols * nb,
+                       lane);
+    __syncwarp();
+    if (row < batch && lane < ncols) {
+      const float v = x[row * features + c0 + lane];
+      const float* t = sm.knots + lane;
+      const float* r = srow + lane * nb;
+      float acc = 0.0f;
+      if (!isfinite(v)) {
+        acc = __int_as_float(0x7fc00000);
+      } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
+        const int i = find_span(t, n_knots, v);
+        float w[2 * kOrder + 2], rw[kOrder][kOrder];
+        load_span<kOrder>(t, sm.recip + lane, n_knots, i, w, rw);
+        float b[kMaxOrder + 1], db[kMaxOrder + 1];
+        span_basis<kOrder, true>(w, rw, n_knots, i, v, b, db);
+#pragma unroll
+        for (int m = 0; m <= kOrder; ++m) {
+          const int j = i - kOrder + m;
+          if (j >= 0 && j < nb) acc = __fadd_rn(acc, __fmul_rn(r[j], db[m]));
+        }
+      }
+      gx[row * features + c0 + lane] = acc;
+    }
+    __syncwarp();
   }
-  gx[e] = acc;
 }
 
 int validate(int64_t batch, int64_t features, int32_t n_knots, int32_t order, int64_t* n) {
@@ -220,33 +321,43 @@ int validate(int64_t batch, int64_t features, int32_t n_knots, int32_t order, in
   return KAT_OK;
 }
 
+// Grid: as many blocks as fit on the GPU at once, never more than there are tiles.
+cudaError_t grid_size(int64_t batch, int64_t features, const void* fn, size_t smem,
+                      unsigned* blocks) {
+  int dev = 0, sms = 0, occ = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess && smem > 48 * 1024)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kBsThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = ((batch + kTileRows - 1) / kTileRows) *
+                        ((features + kTileCols - 1) / kTileCols);
+  *blocks = unsigned(std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sms) * std::max(occ, 1))));
+  return cudaSuccess;
+}
+
 template <int kOrder>
-cudaError_t launch_fwd(const float* x, const float* grid, float* out, int64_t n, int64_t f,
+cudaError_t launch_fwd(const float* x, const float* grid, float* out, int64_t batch, int64_t f,
                        int nk, cudaStream_t s) {
-  const size_t smem = size_t(kBsThreads) * (nk - 1 - kOrder) * sizeof(float);
-  if (smem > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute((const void*)kat_bspline_fwd_kernel<kOrder>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(smem));
-    if (e != cudaSuccess) return e;
-  }
-  const unsigned blocks = unsigned((n + kBsThreads - 1) / kBsThreads);
-  kat_bspline_fwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, out, n, f, nk);
+  const size_t smem = smem_bytes(nk, kOrder);
+  unsigned blocks = 0;
+  const cudaError_t e = grid_size(batch, f, (const void*)kat_bspline_fwd_kernel<kOrder>, smem,
+                                  &blocks);
+  if (e != cudaSuccess) return e;
+  kat_bspline_fwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, out, batch, f, nk);
   return cudaGetLastError();
 }
 
 template <int kOrder>
-cudaError_t launch_bwd(const float* x, const float* grid, const float* gb, float* gx, int64_t n,
-                       int64_t f, int nk, cudaStream_t s) {
-  const size_t smem = size_t(kBsThreads) * (nk - 1 - kOrder) * sizeof(float);
-  if (smem > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute((const void*)kat_bspline_bwd_kernel<kOrder>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(smem));
-    if (e != cudaSuccess) return e;
-  }
-  const unsigned blocks = unsigned((n + kBsThreads - 1) / kBsThreads);
-  kat_bspline_bwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, gb, gx, n, f, nk);
+cudaError_t launch_bwd(const float* x, const float* grid, const float* gb, float* gx,
+                       int64_t batch, int64_t f, int nk, cudaStream_t s) {
+  const size_t smem = smem_bytes(nk, kOrder);
+  unsigned blocks = 0;
+  const cudaError_t e = grid_size(batch, f, (const void*)kat_bspline_bwd_kernel<kOrder>, smem,
+                                  &blocks);
+  if (e != cudaSuccess) return e;
+  kat_bspline_bwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, gb, gx, batch, f, nk);
   return cudaGetLastError();
 }
 
@@ -265,11 +376,11 @@ int kat_bspline_basis_fwd(const float* x, const float* grid, float* bases, int64
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (spline_order) {
-    case 1: e = launch_fwd<1>(x, grid, bases, n, features, n_knots, s); break;
-    case 2: e = launch_fwd<2>(x, grid, bases, n, features, n_knots, s); break;
-    case 3: e = launch_fwd<3>(x, grid, bases, n, features, n_knots, s); break;
-    case 4: e = launch_fwd<4>(x, grid, bases, n, features, n_knots, s); break;
-    default: e = launch_fwd<5>(x, grid, bases, n, features, n_knots, s); break;
+    case 1: e = launch_fwd<1>(x, grid, bases, batch, features, n_knots, s); break;
+    case 2: e = launch_fwd<2>(x, grid, bases, batch, features, n_knots, s); break;
+    case 3: e = launch_fwd<3>(x, grid, bases, batch, features, n_knots, s); break;
+    case 4: e = launch_fwd<4>(x, grid, bases, batch, features, n_knots, s); break;
+    default: e = launch_fwd<5>(x, grid, bases, batch, features, n_knots, s); break;
   }
   return e == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
@@ -286,11 +397,11 @@ int kat_bspline_basis_bwd(const float* x, const float* grid, const float* grad_b
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (spline_order) {
-    case 1: e = launch_bwd<1>(x, grid, grad_bases, grad_x, n, features, n_knots, s); break;
-    case 2: e = launch_bwd<2>(x, grid, grad_bases, grad_x, n, features, n_knots, s); break;
-    case 3: e = launch_bwd<3>(x, grid, grad_bases, grad_x, n, features, n_knots, s); break;
-    case 4: e = launch_bwd<4>(x, grid, grad_bases, grad_x, n, features, n_knots, s); break;
-    default: e = launch_bwd<5>(x, grid, grad_bases, grad_x, n, features, n_knots, s); break;
+    case 1: e = launch_bwd<1>(x, grid, grad_bases, grad_x, batch, features, n_knots, s); break;
+    case 2: e = launch_bwd<2>(x, grid, grad_bases, grad_x, batch, features, n_knots, s); break;
+    case 3: e = launch_bwd<3>(x, grid, grad_bases, grad_x, batch, features, n_knots, s); break;
+    case 4: e = launch_bwd<4>(x, grid, grad_bases, grad_x, batch, features, n_knots, s); break;
+    default: e = launch_bwd<5>(x, grid, grad_bases, grad_x, batch, features, n_knots, s); break;
   }
   return e == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }

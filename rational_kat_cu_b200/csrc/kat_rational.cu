@@ -597,6 +597,8 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
   const int tc = threadIdx.x % p.tile_cols;
   const int tr = threadIdx.x / p.tile_cols;
   if (tr >= p.tile_rows) return;
+  // Programmatic dependent of the previous kernel on the stream: wait for it before reading.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   int64_t i0, i1;
   block_items(p, blockIdx.x, i0, i1);
   const int64_t step = int64_t(p.tile_rows) * p.width;
@@ -744,6 +746,18 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
                "l"(gmem_src)
                : "memory");
 }
+// 8-byte variant (the .cg form copies 16 bytes only): for groups whose width allows 8-byte
+// vectors but not 16-byte ones.
+__device__ __forceinline__ void cp_async8(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+template <int kVB>
+__device__ __forceinline__ void cp_async_vec(void* smem_dst, const void* gmem_src) {
+  if constexpr (kVB == 16) cp_async16(smem_dst, gmem_src); else cp_async8(smem_dst, gmem_src);
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -761,17 +775,21 @@ __device__ __forceinline__ void cp_async_wait() {
 #define KAT_ASYNC_BOUNDS __launch_bounds__(kMaxThreads)
 #endif
 
-template <typename Tio, int kStages, int kRows, int kF>
+template <typename Tio, int kStages, int kRows, int kF, int kVB = 16>
 __global__ void KAT_ASYNC_BOUNDS
 kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __restrict__ dx,
                      const float* __restrict__ num, const float* __restrict__ den,
                      double* __restrict__ partial, const Plan p) {
-  constexpr int V = 16 / sizeof(Tio);
+  constexpr int V = kVB / sizeof(Tio);   // elements per vector (16- or 8-byte vectors)
   constexpr bool kRefine = sizeof(Tio) == 4;
   using L = typename std::conditional<sizeof(Tio) == 4, S2, float2>::type;
-  extern __shared__ __align__(16) uint4 ring[];
+  using Slot = typename BitsOf<kVB>::T;
+  extern __shared__ __align__(16) uint4 ring_words[];
+  Slot* const ring = reinterpret_cast<Slot*>(ring_words);
   const int T = blockDim.x;
   float* s_acc = reinterpret_cast<float*>(ring + size_t(kStages) * kRows * 2 * T);
+  // Programmatic dependent of the previous kernel on the stream: wait for it before reading.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x;
   const int tc = tid % p.tile_cols;
   const int tr = tid / p.tile_cols;
@@ -781,9 +799,9 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
   block_items(p, blockIdx.x, i0, i1);
   const int64_t step = int64_t(p.tile_rows) * p.width;
   const int64_t cb0 = i0 / p.rows;
-  uint4* const ring_t = ring + tid;
-  const int slot_stride = 2 * T;            // uint4s between rows of a stage
-  const int stage_stride = kRows * 2 * T;   // uint4s between stages
+  Slot* const ring_t = ring + tid;
+  const int slot_stride = 2 * T;            // slots between rows of a stage
+  const int stage_stride = kRows * 2 * T;   // slots between stages
 
   for (int64_t i = i0; i < i1;) {
     const int64_t cb = i / p.rows;
@@ -807,12 +825,12 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
       int load_row = 0;
       // Issue the loads of the next batch (rows load_row .. load_row + kRows - 1).
       auto issue = [&]() {
-        uint4* sp = ring_t + load_stage * stage_stride;
+        Slot* sp = ring_t + load_stage * stage_stride;
 #pragma unroll
         for (int u = 0; u < kRows; ++u) {
           if (load_row + u < n) {
-            cp_async16(sp + u * slot_stride, lx);
-            cp_async16(sp + u * slot_stride + T, lg);
+            cp_async_vec<kVB>(sp + u * slot_stride, lx);
+            cp_async_vec<kVB>(sp + u * slot_stride + T, lg);
             lx += step;
             lg += step;
           }
@@ -828,13 +846,13 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
       for (int b = 0; b < nb; ++b) {
         issue();
         cp_async_wait<kStages - 1>();
-        const uint4* sp = ring_t + use_stage * stage_stride;
+        const Slot* sp = ring_t + use_stage * stage_stride;
 #pragma unroll
         for (int u = 0; u < kRows; ++u) {
           if (b * kRows + u < n) {
-            const uint4 rx = sp[u * slot_stride];
-            const uint4 rg = sp[u * slot_stride + T];
-            const uint4 d = bwd_vec<Tio, V, L, kRefine, kF>(rx, rg, c, acc);
+            const Slot rx = sp[u * slot_stride];
+            const Slot rg = sp[u * slot_stride + T];
+            const Slot d = bwd_vec<Tio, V, L, kRefine, kF>(rx, rg, c, acc);
             if (write_dx) {
               store_raw<Tio, V>(dp, d);
               dp += step;
@@ -918,6 +936,9 @@ kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restric
   const int64_t g = int64_t(blockIdx.x) * kReduceWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (g >= p.num_groups) return;
+  // Launched as a programmatic dependent of the partial-sum kernel: wait here until that grid
+  // has completed and its stores are visible (returns at once for an ordinary launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   double tot[kAcc];
   group_totals(partial, p, g, lane, tot);
   write_group(tot, 1.0, true, g, lane, den, dnum, dden, p.formula);
@@ -1296,6 +1317,8 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nwarps = blockDim.x >> 5;
+  // Programmatic dependent of the partial-sum kernel, as kat_bwd_reduce_kernel.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
     group_totals(partial, p, g, lane, tot);
@@ -1367,6 +1390,34 @@ constexpr int kUnroll = KAT_FWD_UNROLL;
 constexpr int kUnrollBwd = KAT_BWD_UNROLL;
 
 int elem_bytes(int dtype) { return dtype == KAT_DTYPE_F32 ? 4 : 2; }
+
+// Programmatic dependent launch: the forward, the cp.async backward and the grid reductions are
+// launched with programmatic stream serialization, so each can be launched while the previous
+// kernel on the stream drains; each waits (griddepcontrol.wait) before it reads anything.
+// KAT_RATIONAL_PDL=0 launches them as ordinary stream-ordered kernels.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("KAT_RATIONAL_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 int validate_dims(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
                   int64_t* n_elems) {
@@ -1653,9 +1704,9 @@ int plan_for_launch_uncached(const void* fn, int64_t batch, int64_t channels, in
 template <typename Tio, int V, int kF>
 cudaError_t launch_fwd_t(const void* x, void* y, const float* num, const float* den, const Plan& p,
                          cudaStream_t s) {
-  kat_fwd_kernel<Tio, V, kUnroll, kF><<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), 0, s>>>(
-      static_cast<const Tio*>(x), static_cast<Tio*>(y), num, den, p);
-  return cudaGetLastError();
+  return launch_pdl(kat_fwd_kernel<Tio, V, kUnroll, kF>, dim3(unsigned(p.blocks)),
+                    dim3(unsigned(p.threads)), 0, s, static_cast<const Tio*>(x),
+                    static_cast<Tio*>(y), num, den, p);
 }
 
 template <typename Tio, int V, int kF>
@@ -1909,41 +1960,52 @@ constexpr int kAsyncCols = KAT_ASYNC_COLS;
 constexpr int kAsyncStages = KAT_ASYNC_STAGES;
 constexpr int kAsyncRows = KAT_ASYNC_ROWS;
 
-size_t async_smem_bytes(int threads) {
-  return size_t(kAsyncStages) * kAsyncRows * 2 * 16 * threads + size_t(kAcc) * 4 * (threads + 1);
+size_t async_smem_bytes(int threads, int vec_bytes) {
+  return size_t(kAsyncStages) * kAsyncRows * 2 * vec_bytes * threads +
+         size_t(kAcc) * 4 * (threads + 1);
 }
 
-template <int kF>
-const void* bwd_async_kernel_for_f(int dtype) {
+template <int kF, int kVB>
+const void* bwd_async_kernel_for_fv(int dtype) {
   switch (dtype) {
-    case KAT_DTYPE_F32: return (const void*)kat_bwd_async_kernel<float, kAsyncStages, kAsyncRows, kF>;
+    case KAT_DTYPE_F32:
+      return (const void*)kat_bwd_async_kernel<float, kAsyncStages, kAsyncRows, kF, kVB>;
     case KAT_DTYPE_F16:
-      return (const void*)kat_bwd_async_kernel<__half, kAsyncStages, kAsyncRows, kF>;
-    default: return (const void*)kat_bwd_async_kernel<__nv_bfloat16, kAsyncStages, kAsyncRows, kF>;
+      return (const void*)kat_bwd_async_kernel<__half, kAsyncStages, kAsyncRows, kF, kVB>;
+    default:
+      return (const void*)kat_bwd_async_kernel<__nv_bfloat16, kAsyncStages, kAsyncRows, kF, kVB>;
   }
 }
 
-const void* bwd_async_kernel_for(int dtype, int formula) {
-  return formula == kFormulaKat ? bwd_async_kernel_for_f<kFormulaKat>(dtype)
-                                : bwd_async_kernel_for_f<kFormulaAbsSum>(dtype);
+// The cp.async backward for (dtype, formula, vector bytes 16 or 8).
+const void* bwd_async_kernel_for(int dtype, int formula, int vec_bytes = 16) {
+  if (vec_bytes == 16)
+    return formula == kFormulaKat ? bwd_async_kernel_for_fv<kFormulaKat, 16>(dtype)
+                                  : bwd_async_kernel_for_fv<kFormulaAbsSum, 16>(dtype);
+  return formula == kFormulaKat ? bwd_async_kernel_for_fv<kFormulaKat, 8>(dtype)
+                                : bwd_async_kernel_for_fv<kFormulaAbsSum, 8>(dtype);
 }
 
 // Plan of the cp.async backward: occupancy from the kernel's registers and its shared
 // memory at this block size.  Returns -1 when it does not apply.
 int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
-                        int dtype, int formula, int* dev_out, Plan* p);
+                        int dtype, int formula, int vec, int* dev_out, Plan* p);
 
+// `vec` = elements per vector: max_vec_for(dtype) (16-byte vectors) or the 8-byte width.
 int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-               int formula, int* dev_out, Plan* p) {
+               int formula, int* dev_out, Plan* p, int vec = 0) {
   if (pipeline_mode() != 0) return -1;
+  if (vec == 0) vec = max_vec_for(dtype);
+  const int vb = vec * elem_bytes(dtype);
+  if (vb != 16 && vb != 8) return -1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
-  const PlanKey key{dev, bwd_async_kernel_for(dtype, formula), dtype, max_vec_for(dtype), batch, channels,
+  const PlanKey key{dev, bwd_async_kernel_for(dtype, formula, vb), dtype, vec, batch, channels,
                     inner, num_groups};
   PlanEntry e;
   if (!plan_cache_get(key, &e)) {
-    e.status = plan_async_uncached(batch, channels, inner, num_groups, dtype, formula, dev_out,
-                                   &e.plan);
+    e.status = plan_async_uncached(batch, channels, inner, num_groups, dtype, formula, vec,
+                                   dev_out, &e.plan);
     if (e.status == KAT_OK || e.status == -1) plan_cache_put(key, e);
   }
   *dev_out = dev;
@@ -1952,8 +2014,9 @@ int plan_async(int64_t batch, int64_t channels, int64_t inner, int64_t num_group
 }
 
 int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups,
-                        int dtype, int formula, int* dev_out, Plan* p) {
-  const int vmax = max_vec_for(dtype);
+                        int dtype, int formula, int vec, int* dev_out, Plan* p) {
+  const int vmax = vec;
+  const int vb = vec * elem_bytes(dtype);
   const int64_t gw = (channels / num_groups) * inner;
   if (pipeline_mode() != 0 || gw % vmax != 0) return -1;
   int dev = 0;
@@ -1968,8 +2031,8 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
   int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
                           max_cols);
   if (st != KAT_OK) return st;
-  const void* fn = bwd_async_kernel_for(dtype, formula);
-  const size_t smem = async_smem_bytes(probe.threads);
+  const void* fn = bwd_async_kernel_for(dtype, formula, vb);
+  const size_t smem = async_smem_bytes(probe.threads, vb);
   if (smem > size_t(kPipeSmemBudget)) return -1;
   if (allow_dynamic_smem(dev, fn, uint32_t(smem)) != cudaSuccess) return KAT_ERR_CUDA;
   int occ = 1;
@@ -1995,11 +2058,16 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
 template <typename Tio, int kF>
 cudaError_t launch_bwd_async_t(const void* x, const void* gy, void* dx, const float* num,
                                const float* den, double* partial, const Plan& p, cudaStream_t s) {
-  kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows, kF>
-      <<<dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)), async_smem_bytes(p.threads), s>>>(
-          static_cast<const Tio*>(x), static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num,
-          den, partial, p);
-  return cudaGetLastError();
+  const int vb = p.vec * int(sizeof(Tio));
+  if (vb == 16)
+    return launch_pdl(kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows, kF, 16>,
+                      dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)),
+                      async_smem_bytes(p.threads, 16), s, static_cast<const Tio*>(x),
+                      static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num, den, partial, p);
+  return launch_pdl(kat_bwd_async_kernel<Tio, kAsyncStages, kAsyncRows, kF, 8>,
+                    dim3(unsigned(p.blocks)), dim3(unsigned(p.threads)),
+                    async_smem_bytes(p.threads, 8), s, static_cast<const Tio*>(x),
+                    static_cast<const Tio*>(gy), static_cast<Tio*>(dx), num, den, partial, p);
 }
 
 template <int kF>
@@ -2043,9 +2111,12 @@ cudaError_t launch_bwd_tma(int dtype, const void* x, const void* gy, void* dx, c
 int launch_reduce(const void* workspace, const float* den, float* dnum, float* dden,
                   const Plan& p, const Peers* peers, cudaStream_t s) {
   if (peers == nullptr) {
+    // Programmatic dependent launch: the reduction's launch overlaps the tail of the
+    // partial-sum kernel, and griddepcontrol.wait inside it orders the reads.
     const unsigned grid = unsigned((p.num_groups + kReduceWarps - 1) / kReduceWarps);
-    kat_bwd_reduce_kernel<<<dim3(grid), dim3(kReduceWarps * 32), 0, s>>>(
-        static_cast<const double*>(workspace), den, dnum, dden, p);
+    if (launch_pdl(kat_bwd_reduce_kernel, dim3(grid), dim3(kReduceWarps * 32), 0, s,
+                   static_cast<const double*>(workspace), den, dnum, dden, p) != cudaSuccess)
+      return KAT_ERR_CUDA;
   } else {
     const size_t smem = size_t(p.num_groups) * kAcc * sizeof(double);
     if (smem > 48 * 1024) {
@@ -2054,8 +2125,10 @@ int launch_reduce(const void* workspace, const float* den, float* dnum, float* d
           cudaSuccess)
         return KAT_ERR_CUDA;
     }
-    kat_bwd_reduce_exchange_kernel<<<1, dim3(kReduceThreads), smem, s>>>(
-        static_cast<const double*>(workspace), den, dnum, dden, p, *peers);
+    if (launch_pdl(kat_bwd_reduce_exchange_kernel, dim3(1), dim3(kReduceThreads), smem, s,
+                   static_cast<const double*>(workspace), den, dnum, dden, p,
+                   *peers) != cudaSuccess)
+      return KAT_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
@@ -2081,9 +2154,10 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
   const int vec = n == 0 ? 1 : pick_vec(dtype, gw, ptrs, 3);
   if (num_groups > 0x7fffffff) return KAT_ERR_BAD_GROUPS;
   Plan p;
-  if (n != 0 && vec == max_vec_for(dtype)) {
+  // cp.async backward for 16-byte and for 8-byte vectors.
+  if (n != 0 && (vec == max_vec_for(dtype) || vec * elem_bytes(dtype) == 8)) {
     int dev = 0;
-    st = plan_async(batch, channels, inner, num_groups, dtype, formula, &dev, &p);
+    st = plan_async(batch, channels, inner, num_groups, dtype, formula, &dev, &p, vec);
     if (st != -1) {
       if (st != KAT_OK) return st;
       if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
@@ -2340,10 +2414,14 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
     const int t = plan_tma(batch, channels, inner, num_groups, dtype, true, &d, &p, &q);
     if (t == KAT_OK) need = p.workspace_bytes;
     else if (t != -1) st = t;
-    for (int f = kFormulaKat; st == KAT_OK && f <= kFormulaAbsSum; ++f) {
-      const int a = plan_async(batch, channels, inner, num_groups, dtype, f, &d, &p);
-      if (a == KAT_OK) need = std::max<uint64_t>(need, p.workspace_bytes);
-      else if (a != -1) st = a;
+    const int vecs[2] = {max_vec_for(dtype), 8 / elem_bytes(dtype)};
+    for (int v : vecs) {
+      for (int f = kFormulaKat; st == KAT_OK && f <= kFormulaAbsSum; ++f) {
+        if (gw % v != 0) continue;
+        const int a = plan_async(batch, channels, inner, num_groups, dtype, f, &d, &p, v);
+        if (a == KAT_OK) need = std::max<uint64_t>(need, p.workspace_bytes);
+        else if (a != -1) st = a;
+      }
     }
   }
   // Enough for every kernel the backward may pick, for either formula.

@@ -50,3 +50,35 @@ def test_pipeline_mode_parity(mode):
                          timeout=600)
     assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stdout + res.stderr
 
+
+
+HASH_CHILD = r'''
+import sys, hashlib
+sys.path.insert(0, {repo!r})
+import torch
+import rational_kat_cu_b200 as kat
+torch.manual_seed(0)
+x = torch.randn(64, 197, 3072, device="cuda").to(torch.bfloat16).requires_grad_(True)
+m = kat.KAT_Group(num_groups=8, mode="gelu").cuda()
+y = m(x)
+y.backward(torch.randn_like(y))
+torch.cuda.synchronize()
+h = hashlib.sha256()
+for t in (y, x.grad, m.weight_numerator.grad, m.weight_denominator.grad):
+    h.update(t.detach().float().cpu().numpy().tobytes())
+print("hash", h.hexdigest())
+'''
+
+
+def test_grid_reduction_launch_modes_agree():
+    """The grid reduction launched as a programmatic dependent of the partial-sum kernel
+    (default) and as an ordinary launch (KAT_RATIONAL_PDL=0) give bit-identical results."""
+    code = HASH_CHILD.format(repo=REPO)
+    hashes = []
+    for pdl in ("1", "0"):
+        env = dict(os.environ, KAT_RATIONAL_PDL=pdl)
+        res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True,
+                             text=True, timeout=600)
+        assert res.returncode == 0, res.stdout + res.stderr
+        hashes.append([l for l in res.stdout.splitlines() if l.startswith("hash")][-1])
+    assert hashes[0] == hashes[1]
