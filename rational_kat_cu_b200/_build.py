@@ -1,6 +1,6 @@
 """Build recipe for libkat_rational.so (the sm_100a kernels behind the C ABI).
 
-`build()` runs nvcc on csrc/kat_rational.cu and csrc/kat_bspline.cu for
+`build()` runs nvcc on csrc/kat_rational.cu, csrc/kat_bspline.cu and csrc/kat_gemm.cu for
 `-gencode arch=compute_100a,code=sm_100a` and writes the shared library next to this file, so
 it travels with the source tree.  It rebuilds only when a source or a public header is newer
 than the library.
@@ -16,9 +16,12 @@ import sys
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 SOURCES = [os.path.join(PKG_DIR, "csrc", "kat_rational.cu"),
-           os.path.join(PKG_DIR, "csrc", "kat_bspline.cu")]
+           os.path.join(PKG_DIR, "csrc", "kat_bspline.cu"),
+           os.path.join(PKG_DIR, "csrc", "kat_gemm.cu")]
 HEADERS = [os.path.join(REPO_DIR, "include", "kat_rational.h"),
-           os.path.join(REPO_DIR, "include", "kat_bspline.h")]
+           os.path.join(REPO_DIR, "include", "kat_bspline.h"),
+           os.path.join(REPO_DIR, "include", "kat_gemm.h"),
+           os.path.join(PKG_DIR, "csrc", "kat_math.cuh")]
 LIBRARY = os.path.join(PKG_DIR, "libkat_rational.so")
 
 NVCC_FLAGS = [

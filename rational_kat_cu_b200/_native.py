@@ -1,5 +1,5 @@
-"""ctypes binding of libkat_rational.so (the C ABI declared in include/kat_rational.h and
-include/kat_bspline.h).
+"""ctypes binding of libkat_rational.so (the C ABI declared in include/kat_rational.h,
+include/kat_bspline.h and include/kat_gemm.h).
 
 The library is loaded once, on first use.  If it is missing the call fails with a
 RuntimeError naming the build command: there is no fallback implementation.
@@ -52,6 +52,11 @@ EXPORTED_SYMBOLS = (
     "kat_rational_exchange_open",
     "kat_rational_exchange_close",
     "kat_rational_exchange_destroy",
+    "kat_gemm_bf16",
+    "kat_gemm_rational_fwd",
+    "kat_gemm_rational_bwd_workspace_bytes",
+    "kat_gemm_rational_bwd",
+    "kat_gemm_device_status",
 )
 
 KAT_MAX_PEERS = 8
@@ -128,6 +133,18 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_bwd_formula.restype = i32
     lib.kat_rational_fwd_f64.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i32, vp]
     lib.kat_rational_fwd_f64.restype = i32
+    lib.kat_gemm_bf16.argtypes = [vp, vp, vp, vp, i64, i64, i64, vp]
+    lib.kat_gemm_bf16.restype = i32
+    lib.kat_gemm_rational_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, i64,
+                                          ctypes.c_int32, ctypes.c_int32, vp]
+    lib.kat_gemm_rational_fwd.restype = i32
+    lib.kat_gemm_rational_bwd_workspace_bytes.argtypes = [i64, i64, ctypes.c_int32, i32]
+    lib.kat_gemm_rational_bwd_workspace_bytes.restype = ctypes.c_size_t
+    lib.kat_gemm_rational_bwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_size_t,
+                                          i64, i64, i64, ctypes.c_int32, ctypes.c_int32, vp]
+    lib.kat_gemm_rational_bwd.restype = i32
+    lib.kat_gemm_device_status.argtypes = [i32, i32, ctypes.POINTER(ctypes.c_int)]
+    lib.kat_gemm_device_status.restype = i32
     lib.kat_bspline_basis_fwd.argtypes = [vp, vp, vp, i64, i64, ctypes.c_int32, ctypes.c_int32,
                                           vp]
     lib.kat_bspline_basis_fwd.restype = i32

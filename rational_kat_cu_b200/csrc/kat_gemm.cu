@@ -1,0 +1,839 @@
+// kat_gemm.cu — sm_100a tensor-core GEMM (C = A B^T, bf16 in, fp32 accumulate) with the
+// group-rational activation fused into its epilogue (C ABI: include/kat_gemm.h).
+//
+// One persistent CTA per SM, 192 threads in three roles:
+//   warp 0, one lane   TMA producer: per k-block, a 128 x 64 tile of A and a 256 x 64 tile of B
+//                      (bf16, 128-byte swizzled rows) into a ring of shared-memory stages;
+//   warp 1, one lane   MMA issuer: tcgen05.mma (kind::f16, M = 128, N = 256, K = 16) from the
+//                      stage's shared-memory descriptors into one of two 256-column fp32
+//                      accumulators in tensor memory; tcgen05.commit frees the stage when its
+//                      MMAs have read it and, after the last k-block, hands the accumulator to
+//                      the epilogue.  Warp 1 also allocates and frees the 512 TMEM columns;
+//   warps 2-5          epilogue: thread r of the 128 owns accumulator row r (TMEM lane r; a
+//                      warp may read only its lane quadrant, warp % 4), reads 32 columns at a
+//                      time with tcgen05.ld, applies the epilogue, writes the bf16 results into
+//                      a 64-byte-swizzled staging tile and one thread stores the tile with TMA.
+// With two accumulators the epilogue of one output tile overlaps the mainloop of the next.
+// Tiles are numbered row-block-major (12 consecutive tiles share a 128-row block of A) and
+// CTA c takes tiles c, c + grid, c + 2 grid, ...
+//
+// Epilogues: plain (C = bf16(acc + bias)); forward (h = bf16(acc + bias), y = rational(h) with
+// the activation kernels' per-element math, so y is bit-identical to kat_rational_fwd on h);
+// backward (g = bf16(acc), h streamed in by TMA, dh = the activation kernels' per-element
+// backward on (h, g), per-thread fp32 gradient sums flushed in a fixed order into per-warp fp64
+// partials, then a second kernel adds the partials of all warps in a fixed order).
+//
+// Every mbarrier wait is bounded (about two seconds of clock cycles).  A wait that runs out
+// sets the CTA's abort flag and the sticky device status word; the other roles see the flag
+// in their own waits and stop, the MMA issuer drains its outstanding MMAs and warp 1 frees the
+// tensor memory before the CTA exits.
+
+#include <cuda.h>  // CUtensorMap and its enums (types only: the encoder is fetched at run time)
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "kat_rational.h"
+#include "kat_gemm.h"
+
+namespace {
+
+#include "kat_math.cuh"
+
+constexpr int kBM = 128;       // tile rows (MMA M, TMEM lanes)
+constexpr int kBN = 256;       // tile columns (MMA N, TMEM columns per accumulator)
+constexpr int kBK = 64;        // k-block: 64 bf16 = one 128-byte swizzle row
+constexpr int kUmmaK = 16;     // K of one kind::f16 MMA
+constexpr int kChunk = 32;     // epilogue columns per tcgen05.ld
+constexpr int kChunks = kBN / kChunk;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr int kEpiWarp0 = 2;
+constexpr uint32_t kTmemCols = 2 * kBN;
+constexpr uint32_t kABytes = kBM * kBK * 2;
+constexpr uint32_t kBBytes = kBN * kBK * 2;
+constexpr uint32_t kChunkBytes = kBM * kChunk * 2;  // 128 rows x 64 bytes
+constexpr int kHBufs = 4;                          // backward: h chunks in flight
+constexpr uint32_t kBarBytes = 256;
+constexpr long long kWaitCycles = 4000000000LL;
+constexpr int kStatusWaitTimeout = KAT_DEVICE_WAIT_TIMEOUT;
+
+enum Mode { kPlain = 0, kFwd = 1, kBwd = 2 };
+
+template <int kMode> struct Cfg;
+template <> struct Cfg<kPlain> {
+  static constexpr int kStages = 4, kOuts = 1, kH = 0;
+};
+template <> struct Cfg<kFwd> {
+  static constexpr int kStages = 4, kOuts = 2, kH = 0;
+};
+template <> struct Cfg<kBwd> {
+  static constexpr int kStages = 3, kOuts = 1, kH = kHBufs;
+};
+
+template <int kMode>
+constexpr uint32_t smem_bytes() {
+  return 1024 + Cfg<kMode>::kStages * (kABytes + kBBytes) +
+         2 * Cfg<kMode>::kOuts * kChunkBytes + Cfg<kMode>::kH * kChunkBytes + kBarBytes;
+}
+static_assert(smem_bytes<kFwd>() <= 227 * 1024, "forward shared memory");
+static_assert(smem_bytes<kBwd>() <= 227 * 1024, "backward shared memory");
+
+struct GemmArgs {
+  int32_t n_tiles;      // column tiles (N / 256)
+  int32_t num_tiles;    // row tiles x column tiles
+  int32_t k_blocks;     // K / 64
+  int32_t group_width;  // N / G (multiple of 32)
+  int32_t groups;
+  const uint16_t* bias;   // bf16 [N] or null
+  const float* num;       // [G, 6]
+  const float* den;       // [G, 4]
+  double* partial;        // backward: [grid][4][G][10]
+};
+
+__device__ int g_gemm_status;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait of one thread for the phase with `parity`; false when the CTA aborted or this
+// wait ran out (which aborts the CTA).
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort = 1;
+      atomicExch(&g_gemm_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(kPending) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
+               : "memory");
+}
+// D[tmem] (+)= A[smem] B[smem]^T for one K = 16 slice.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
+      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+        "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major bf16 tile with 128-byte rows, 128-byte swizzle,
+// 8-row groups 1024 bytes apart (tcgen05 descriptor: start >> 4 in bits 0-13, leading byte
+// offset 16 >> 4 in 16-29 (unused by swizzled K-major layouts), stride byte offset 1024 >> 4 in
+// 32-45, descriptor version 1 in 46-47, swizzle mode 2 = 128B in 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+// Instruction descriptor: fp32 accumulator (bits 4-5 = 1), A and B bf16 (7-9 = 1, 10-12 = 1),
+// both K-major (15, 16 = 0), N >> 3 in 17-22, M >> 4 in 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
+                            (uint32_t(kBM >> 4) << 24);
+
+// Byte offset of 16-byte granule j (0..3) of row r in a 64-byte-swizzled tile (the TMA
+// SWIZZLE_64B pattern: granule index XOR address bits 7-8).
+__device__ __forceinline__ uint32_t sw64_offset(int r, int j) {
+  return uint32_t(r) * 64u + uint32_t((j ^ ((r >> 1) & 3)) << 4);
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) {
+  return __uint_as_float(bits16 << 16);
+}
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+
+template <int kMode, int kF>
+__global__ void __launch_bounds__(kThreads, 1)
+kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const __grid_constant__ CUtensorMap tm_out0,
+                const __grid_constant__ CUtensorMap tm_out1,
+                const __grid_constant__ CUtensorMap tm_h, const GemmArgs args) {
+  constexpr int S = Cfg<kMode>::kStages;
+  constexpr int kOuts = Cfg<kMode>::kOuts;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = s_a + S * kABytes;
+  uint8_t* s_out = s_b + S * kBBytes;                    // [2 buffers][kOuts] chunk tiles
+  uint8_t* s_h = s_out + 2 * kOuts * kChunkBytes;        // backward: [kHBufs] chunk tiles
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + Cfg<kMode>::kH * kChunkBytes);
+  uint64_t* full = bars;              // [S]  TMA -> MMA
+  uint64_t* empty = full + S;         // [S]  MMA -> TMA
+  uint64_t* tfull = empty + S;        // [2]  MMA -> epilogue
+  uint64_t* tempty = tfull + 2;       // [2]  epilogue -> MMA
+  uint64_t* hbar = tempty + 2;        // [kHBufs] backward h loads
+  uint64_t* drain = hbar + kHBufs;    // MMA completion before teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* epi_ok = abort + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(tfull + j, 1);
+      mbar_init(tempty + j, kEpiThreads);
+    }
+    for (int j = 0; j < kHBufs; ++j) mbar_init(hbar + j, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    *epi_ok = 1;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_map(&tm_a);
+    prefetch_map(&tm_b);
+    prefetch_map(&tm_out0);
+    if (kMode == kFwd) prefetch_map(&tm_out1);
+    if (kMode == kBwd) prefetch_map(&tm_h);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = args.n_tiles;
+  const int num_tiles = args.num_tiles;
+  const int k_blocks = args.k_blocks;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * kBM;
+        const int n0 = (tile % n_tiles) * kBN;
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!wait_phase(empty + stage, phase ^ 1u, abort)) { ok = false; break; }
+          mbar_expect_tx(full + stage, kABytes + kBBytes);
+          tma_load_2d(s_a + stage * kABytes, &tm_a, full + stage, kb * kBK, m0);
+          tma_load_2d(s_b + stage * kBBytes, &tm_b, full + stage, kb * kBK, n0);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_phase(tempty + acc, acc_phase ^ 1u, abort)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * kBN);
+        bool ok = true;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!wait_phase(full + stage, phase, abort)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a_desc = sw128_desc(smem_u32(s_a + stage * kABytes));
+          const uint64_t b_desc = sw128_desc(smem_u32(s_b + stage * kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // advance the start address by k x 32 bytes inside the swizzled 128-byte rows
+            umma_bf16(d_tmem, a_desc + uint64_t(k * 2), b_desc + uint64_t(k * 2), kIdesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          }
+          issued = true;
+          umma_commit(empty + stage);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(tfull + acc);
+      }
+      if (issued) {
+        // Every MMA has completed before warp 1 frees the tensor memory (bounded by the clock
+        // alone: on the normal path this returns at once).
+        umma_commit(drain);
+        const long long t0 = clock64();
+        while (!mbar_try(drain, 0)) {
+          if (clock64() - t0 > kWaitCycles) {
+            atomicExch(&g_gemm_status, kStatusWaitTimeout);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;          // accumulator row within the tile
+    const int et = threadIdx.x - kEpiWarp0 * 32;
+    const uint32_t lane_addr = tmem_base + (uint32_t(quad * 32) << 16);
+    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int total_chunks = my_tiles * kChunks;
+
+    double* wpart = nullptr;
+    if constexpr (kMode == kBwd) {
+      wpart = args.partial + (size_t(blockIdx.x) * 4 + (warp - kEpiWarp0)) * size_t(args.groups) * kAcc;
+      for (int i = lane; i < args.groups * kAcc; i += 32) wpart[i] = 0.0;
+      __syncwarp();
+    }
+    // h chunk q lives at tile blockIdx.x + (q / kChunks) * grid, columns (q % kChunks) * 32.
+    auto issue_h = [&](int q) {
+      if constexpr (kMode == kBwd) {
+        const int tile = blockIdx.x + (q / kChunks) * gridDim.x;
+        const int m0 = (tile / n_tiles) * kBM;
+        const int n0 = (tile % n_tiles) * kBN + (q % kChunks) * kChunk;
+        uint64_t* bar = hbar + (q % kHBufs);
+        mbar_expect_tx(bar, kChunkBytes);
+        tma_load_2d(s_h + (q % kHBufs) * kChunkBytes, &tm_h, bar, n0, m0);
+      }
+    };
+    if (kMode == kBwd && et == 0) {
+      for (int q = 0; q < kHBufs && q < total_chunks; ++q) issue_h(q);
+    }
+
+    FwdCoef<float2> fc;
+    BwdCoef<float2> bc;
+    float2 acc_g[kAcc];
+#pragma unroll
+    for (int k = 0; k < kAcc; ++k) acc_g[k] = make_float2(0.0f, 0.0f);
+    int cur_group = -1;
+
+    // Fixed-order flush of this warp's gradient sums for `g` into its fp64 partial row.
+    auto flush = [&](int g) {
+      double tot[kAcc];
+#pragma unroll
+      for (int k = 0; k < kAcc; ++k) {
+        double v = double(acc_g[k].x) + double(acc_g[k].y);
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+        tot[k] = v;
+        acc_g[k] = make_float2(0.0f, 0.0f);
+      }
+      double mine = 0.0;
+#pragma unroll
+      for (int k = 0; k < kAcc; ++k)
+        if (lane == k) mine = tot[k];
+      if (lane < kAcc) wpart[size_t(g) * kAcc + lane] += mine;
+    };
+
+    int q = 0;
+    int local = 0;
+    bool alive = true;
+    for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      const int m0 = (tile / n_tiles) * kBM;
+      const int tile_n0 = (tile % n_tiles) * kBN;
+      for (int c = 0; c < kChunks; ++c, ++q) {
+        const int n0 = tile_n0 + c * kChunk;
+        const int buf = q & 1;
+        // One thread waits (bounded) for what this chunk needs; the barrier below publishes
+        // the outcome so the 128 threads leave together.
+        if (et == 0) {
+          bool ok = true;
+          if (c == 0) ok = wait_phase(tfull + acc, acc_phase, abort);
+          if (kMode == kBwd && ok) ok = wait_phase(hbar + (q % kHBufs), (q / kHBufs) & 1, abort);
+          bulk_wait_read<1>();  // staging buffer `buf` (used two chunks ago) has been read
+          *epi_ok = ok ? 1 : 0;
+        }
+        epi_bar();
+        if (!*epi_ok) { alive = false; break; }
+        if (c == 0) {
+          (void)mbar_try(tfull + acc, acc_phase);  // completed: acquire for this thread
+          tc_fence_after();
+        }
+        uint32_t v[32];
+        tmem_ld32(lane_addr + uint32_t(acc * kBN + c * kChunk), v);
+        if (c == kChunks - 1) {
+          tc_fence_before();
+          mbar_arrive(tempty + acc);
+        }
+        uint8_t* stage0 = s_out + (buf * kOuts) * kChunkBytes;
+        uint32_t w0[16];
+        uint32_t w1[16];
+        if constexpr (kMode == kPlain || kMode == kFwd) {
+          float bias[32];
+          if (args.bias != nullptr) {
+            const uint4* bp = reinterpret_cast<const uint4*>(args.bias + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint4 u = __ldg(bp + j);
+              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                bias[j * 8 + t * 2] = bf16_bits_to_float(uw[t] & 0xFFFFu);
+                bias[j * 8 + t * 2 + 1] = bf16_bits_to_float(uw[t] >> 16);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) bias[j] = 0.0f;
+          }
+          if constexpr (kMode == kFwd) {
+            const int g = n0 / args.group_width;
+            if (g != cur_group) {
+              cur_group = g;
+              load_fwd_coef<float2, kF>(args.num, args.den, g, fc);
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const float2 hv = make_float2(__fadd_rn(__uint_as_float(v[2 * p]), bias[2 * p]),
+                                          __fadd_rn(__uint_as_float(v[2 * p + 1]), bias[2 * p + 1]));
+            w0[p] = Codec<__nv_bfloat16>::pack_word(hv);
+            if constexpr (kMode == kFwd) {
+              const float2 hx = Codec<__nv_bfloat16>::unpack_word(w0[p]);
+              w1[p] = Codec<__nv_bfloat16>::pack_word(fwd_math<float2, false, kF>(hx, fc));
+            }
+          }
+        } else {
+          const int g = n0 / args.group_width;
+          if (g != cur_group) {
+            if (cur_group >= 0) flush(cur_group);
+            cur_group = g;
+            load_bwd_coef<float2, kF>(args.num, args.den, g, bc);
+          }
+          (void)mbar_try(hbar + (q % kHBufs), (q / kHBufs) & 1);  // completed: acquire
+          const uint8_t* hrow = s_h + (q % kHBufs) * kChunkBytes;
+          uint32_t hw[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(hrow + sw64_offset(row, j));
+            hw[j * 4 + 0] = u.x; hw[j * 4 + 1] = u.y; hw[j * 4 + 2] = u.z; hw[j * 4 + 3] = u.w;
+          }
+#pragma unroll
+          for (int p = 0; p < 16; ++p) {
+            const uint32_t gw = Codec<__nv_bfloat16>::pack_word(
+                make_float2(__uint_as_float(v[2 * p]), __uint_as_float(v[2 * p + 1])));
+            const float2 go = Codec<__nv_bfloat16>::unpack_word(gw);
+            const float2 x = Codec<__nv_bfloat16>::unpack_word(hw[p]);
+            w0[p] = Codec<__nv_bfloat16>::pack_word(bwd_math<float2, false, kF>(x, go, bc, acc_g));
+          }
+        }
+        // Staging tile(s), 64-byte swizzled rows, then one TMA store per output.
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(stage0 + sw64_offset(row, j)) =
+              make_uint4(w0[j * 4], w0[j * 4 + 1], w0[j * 4 + 2], w0[j * 4 + 3]);
+        if constexpr (kMode == kFwd) {
+          uint8_t* stage1 = stage0 + kChunkBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(stage1 + sw64_offset(row, j)) =
+                make_uint4(w1[j * 4], w1[j * 4 + 1], w1[j * 4 + 2], w1[j * 4 + 3]);
+        }
+        fence_async_shared();
+        epi_bar();
+        if (et == 0) {
+          tma_store_2d(&tm_out0, stage0, n0, m0);
+          if constexpr (kMode == kFwd) tma_store_2d(&tm_out1, stage0 + kChunkBytes, n0, m0);
+          bulk_commit();
+          if (kMode == kBwd && q + kHBufs < total_chunks) issue_h(q + kHBufs);
+        }
+      }
+    }
+    if constexpr (kMode == kBwd) {
+      if (alive && cur_group >= 0) flush(cur_group);
+    }
+    if (et == 0) bulk_wait_all();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_free(tmem_base, kTmemCols);
+  }
+}
+
+// Coefficient gradients: one warp per group adds the partial rows of every (CTA, epilogue
+// warp) in a fixed order (lane-strided, then a fixed shuffle tree) and writes d_num / d_den
+// with the sign conventions of the activation kernels.
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(kReduceWarps * 32)
+kat_gemm_reduce_kernel(const double* __restrict__ partial, int rows, int groups,
+                       const float* __restrict__ den, float* __restrict__ d_num,
+                       float* __restrict__ d_den, int formula) {
+  const int g = blockIdx.x * kReduceWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (g >= groups) return;
+  double tot[kAcc];
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k) tot[k] = 0.0;
+  for (int r = lane; r < rows; r += 32) {
+    const double* src = partial + (size_t(r) * groups + g) * kAcc;
+#pragma unroll
+    for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
+  }
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) tot[k] += __shfl_xor_sync(0xffffffffu, tot[k], m);
+  }
+  double v = 0.0;
+#pragma unroll
+  for (int k = 0; k < kAcc; ++k)
+    if (lane == k) v = tot[k];
+  if (lane >= kAcc) return;
+  const float f = float(v);
+  if (lane < 6) {
+    d_num[g * 6 + lane] = f;
+  } else {
+    float sg = 1.0f;
+    if (formula == kFormulaKat) {
+      const float b = den[g * 4 + (lane - 6)];
+      sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
+    }
+    d_den[g * 4 + (lane - 6)] = -(sg * f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Row-major bf16 [rows, cols] matrix, box of box_rows x box_cols elements.
+bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, uint32_t box_cols,
+              uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encoder();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= 64) return 0;
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+      return 0;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_shape(int64_t m, int64_t n, int64_t k) {
+  if (m < 1 || n < kBN || k < kBK) return KAT_ERR_BAD_SHAPE;
+  if (n % kBN != 0 || k % kBK != 0) return KAT_ERR_BAD_SHAPE;
+  if (m >= (int64_t(1) << 31) || n >= (int64_t(1) << 31) || k >= (int64_t(1) << 31))
+    return KAT_ERR_BAD_SHAPE;
+  const int64_t tiles = ((m + kBM - 1) / kBM) * (n / kBN);
+  if (tiles >= (int64_t(1) << 31)) return KAT_ERR_BAD_SHAPE;
+  return KAT_OK;
+}
+
+int check_groups(int64_t n, int32_t groups) {
+  if (groups < 1 || n % groups != 0 || (n / groups) % kChunk != 0) return KAT_ERR_BAD_GROUPS;
+  return KAT_OK;
+}
+
+int grid_for(int64_t m, int64_t n, int device) {
+  const int64_t tiles = ((m + kBM - 1) / kBM) * (n / kBN);
+  const int sms = sm_count(device);
+  if (sms <= 0) return 0;
+  return int(tiles < sms ? tiles : sms);
+}
+
+template <int kMode, int kF>
+int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o0,
+           const CUtensorMap& o1, const CUtensorMap& h, const GemmArgs& args, int grid,
+           cudaStream_t stream) {
+  auto kernel = kat_gemm_kernel<kMode, kF>;
+  constexpr uint32_t smem = smem_bytes<kMode>();
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return KAT_ERR_CUDA;
+  kernel<<<grid, kThreads, smem, stream>>>(a, b, o0, o1, h, args);
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+int current_device(int* dev) { return cudaGetDevice(dev) == cudaSuccess ? KAT_OK : KAT_ERR_CUDA; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI.
+// ---------------------------------------------------------------------------
+
+extern "C" {
+
+int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c, int64_t m, int64_t n,
+                  int64_t k, void* stream) {
+  if (a == nullptr || b == nullptr || c == nullptr) return KAT_ERR_NULL_POINTER;
+  if (int st = check_shape(m, n, k)) return st;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c) || (bias != nullptr && !aligned16(bias)))
+    return KAT_ERR_BAD_SHAPE;
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  const int grid = grid_for(m, n, dev);
+  if (grid <= 0) return KAT_ERR_CUDA;
+  CUtensorMap ma, mb, mc;
+  if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mc, c, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+    return KAT_ERR_CUDA;
+  GemmArgs args{};
+  args.n_tiles = int32_t(n / kBN);
+  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
+  args.k_blocks = int32_t(k / kBK);
+  args.group_width = int32_t(n);
+  args.groups = 1;
+  args.bias = static_cast<const uint16_t*>(bias);
+  return launch<kPlain, kFormulaKat>(ma, mb, mc, mc, mc, args, grid,
+                                     static_cast<cudaStream_t>(stream));
+}
+
+int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const float* num,
+                          const float* den, void* h, void* y, int64_t m, int64_t n, int64_t k,
+                          int32_t num_groups, int32_t formula, void* stream) {
+  if (a == nullptr || b == nullptr || num == nullptr || den == nullptr || h == nullptr ||
+      y == nullptr)
+    return KAT_ERR_NULL_POINTER;
+  if (formula != KAT_FORMULA_KAT && formula != KAT_FORMULA_ABS_SUM) return KAT_ERR_BAD_FORMULA;
+  if (int st = check_shape(m, n, k)) return st;
+  if (int st = check_groups(n, num_groups)) return st;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(h) || !aligned16(y) ||
+      (bias != nullptr && !aligned16(bias)))
+    return KAT_ERR_BAD_SHAPE;
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  const int grid = grid_for(m, n, dev);
+  if (grid <= 0) return KAT_ERR_CUDA;
+  CUtensorMap ma, mb, mh, my;
+  if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mh, h, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&my, y, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+    return KAT_ERR_CUDA;
+  GemmArgs args{};
+  args.n_tiles = int32_t(n / kBN);
+  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
+  args.k_blocks = int32_t(k / kBK);
+  args.group_width = int32_t(n / num_groups);
+  args.groups = num_groups;
+  args.bias = static_cast<const uint16_t*>(bias);
+  args.num = num;
+  args.den = den;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return formula == KAT_FORMULA_KAT
+             ? launch<kFwd, kFormulaKat>(ma, mb, mh, my, mh, args, grid, st)
+             : launch<kFwd, kFormulaAbsSum>(ma, mb, mh, my, mh, args, grid, st);
+}
+
+size_t kat_gemm_rational_bwd_workspace_bytes(int64_t m, int64_t n, int32_t num_groups,
+                                             int device) {
+  if (check_shape(m, n, kBK) != KAT_OK || num_groups < 1) return 0;
+  const int grid = grid_for(m, n, device);
+  if (grid <= 0) return 0;
+  return size_t(grid) * 4 * size_t(num_groups) * kAcc * sizeof(double);
+}
+
+int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const float* num,
+                          const float* den, void* dh, float* d_num, float* d_den,
+                          void* workspace, size_t workspace_bytes, int64_t m, int64_t n,
+                          int64_t k, int32_t num_groups, int32_t formula, void* stream) {
+  if (a == nullptr || b == nullptr || h == nullptr || num == nullptr || den == nullptr ||
+      dh == nullptr || d_num == nullptr || d_den == nullptr)
+    return KAT_ERR_NULL_POINTER;
+  if (formula != KAT_FORMULA_KAT && formula != KAT_FORMULA_ABS_SUM) return KAT_ERR_BAD_FORMULA;
+  if (int st = check_shape(m, n, k)) return st;
+  if (int st = check_groups(n, num_groups)) return st;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(h) || !aligned16(dh)) return KAT_ERR_BAD_SHAPE;
+  int dev = 0;
+  if (int st = current_device(&dev)) return st;
+  const int grid = grid_for(m, n, dev);
+  if (grid <= 0) return KAT_ERR_CUDA;
+  const size_t need = size_t(grid) * 4 * size_t(num_groups) * kAcc * sizeof(double);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return KAT_ERR_WORKSPACE;
+  CUtensorMap ma, mb, mh, md;
+  if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mh, h, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&md, dh, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+    return KAT_ERR_CUDA;
+  GemmArgs args{};
+  args.n_tiles = int32_t(n / kBN);
+  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
+  args.k_blocks = int32_t(k / kBK);
+  args.group_width = int32_t(n / num_groups);
+  args.groups = num_groups;
+  args.num = num;
+  args.den = den;
+  args.partial = static_cast<double*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = formula == KAT_FORMULA_KAT
+                     ? launch<kBwd, kFormulaKat>(ma, mb, md, md, mh, args, grid, st)
+                     : launch<kBwd, kFormulaAbsSum>(ma, mb, md, md, mh, args, grid, st);
+  if (rc != KAT_OK) return rc;
+  const int rgrid = (num_groups + kReduceWarps - 1) / kReduceWarps;
+  kat_gemm_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, st>>>(
+      static_cast<const double*>(workspace), grid * 4, num_groups, den, d_num, d_den, formula);
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+int kat_gemm_device_status(int device, int reset, int* status) {
+  if (status == nullptr) return KAT_ERR_NULL_POINTER;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return KAT_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return KAT_ERR_CUDA;
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(int));
+  if (e == cudaSuccess && reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int));
+  }
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return KAT_ERR_CUDA;
+  *status = v;
+  return KAT_OK;
+}
+
+}  // extern "C"

@@ -13,7 +13,10 @@ around it is the standard ViT-B/16 layout, written here in plain PyTorch (no tim
   class token (1000 classes).
 
 At batch 128, act1 sees [128, 197, 768] and act2 [128, 197, 3072] in every block.  Attention
-uses torch's scaled_dot_product_attention; the linear layers are cuBLAS GEMMs.
+uses torch's scaled_dot_product_attention; the linear layers are cuBLAS GEMMs, except that with
+`fused_gemm=True` the KAN block's fc1 -> act2 -> fc2 runs on the tcgen05 GEMMs with act2 in
+their epilogues (fused_gemm.KANMlpFused: act2's forward in fc1's epilogue, its backward in the
+epilogue of fc2's input-gradient GEMM).
 
 Training step: cross-entropy on the class logits, backward, optimizer step.  Data parallel
 is one process per GPU with DistributedDataParallel over NCCL; the KAT coefficient
@@ -32,6 +35,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import fused_gemm
 from .kat_1dgroup import KAT_Group
 
 
@@ -48,6 +52,7 @@ class ViTConfig:
     num_groups: int = 8          # KAT_Group groups
     drop: float = 0.0
     act: str = "kat"             # "kat" (GR-KAN) or "gelu" (plain ViT MLP)
+    fused_gemm: bool = False     # KAN block: act2 in the fc1 / fc2-dgrad GEMM epilogues
 
     @property
     def num_tokens(self) -> int:
@@ -64,7 +69,8 @@ class KAN(nn.Module):
     act1 -> drop -> fc1 -> act2 -> drop -> fc2, act1 initialised 'identity', act2 'gelu'."""
 
     def __init__(self, in_features: int, hidden_features: int, num_groups: int = 8,
-                 act_init=("identity", "gelu"), drop: float = 0.0, device: str = "cuda"):
+                 act_init=("identity", "gelu"), drop: float = 0.0, device: str = "cuda",
+                 fused_gemm: bool = False):
         super().__init__()
         self.act1 = KAT_Group(num_groups=num_groups, mode=act_init[0], device=device)
         self.drop1 = nn.Dropout(drop)
@@ -72,10 +78,24 @@ class KAN(nn.Module):
         self.act2 = KAT_Group(num_groups=num_groups, mode=act_init[1], device=device)
         self.drop2 = nn.Dropout(drop)
         self.fc2 = nn.Linear(hidden_features, in_features)
+        self.fused_gemm = fused_gemm
+
+    def _fusable(self, x: torch.Tensor) -> bool:
+        """The fused GEMM path applies to bf16 CUDA activations and weights, without dropout
+        between act2 and fc2 and without act2's in-kernel gradient exchange."""
+        return (self.fused_gemm and x.is_cuda and x.dtype == torch.bfloat16
+                and self.fc1.weight.dtype == torch.bfloat16
+                and self.fc2.weight.dtype == torch.bfloat16
+                and (self.drop2.p == 0.0 or not self.training)
+                and getattr(self.act2, "exchange", None) is None
+                and fused_gemm.supports(x.numel() // x.shape[-1], self.fc1.out_features,
+                                        self.fc1.in_features, self.act2.num_groups))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x = self.act1(x)
         x = self.drop1(x)
+        if self._fusable(x):
+            return fused_gemm.kan_mlp_fused(x, self.fc1, self.act2, self.fc2)
         x = self.fc1(x)
         x = self.act2(x)
         x = self.drop2(x)
@@ -119,7 +139,8 @@ class Block(nn.Module):
         self.attn = Attention(dim, cfg.num_heads)
         self.norm2 = nn.LayerNorm(dim, eps=1e-6)
         if cfg.act == "kat":
-            self.mlp = KAN(dim, hidden, cfg.num_groups, drop=cfg.drop, device=kat_device)
+            self.mlp = KAN(dim, hidden, cfg.num_groups, drop=cfg.drop, device=kat_device,
+                           fused_gemm=cfg.fused_gemm)
         else:
             self.mlp = GeluMLP(dim, hidden, cfg.drop)
 

@@ -72,6 +72,37 @@ def test_formula_entry_points_validate_before_launch():
     assert "formula" in _native.strerror(_native.KAT_ERR_BAD_FORMULA)
 
 
+def test_gemm_entry_points_validate_before_launch():
+    lib = _native.lib()
+    E = _native
+    P = 16  # an aligned address value; every call below has a bad argument, so none is used
+    for m, n, k in ((0, 256, 64), (128, 255, 64), (128, 256, 63), (128, 0, 64),
+                    (1 << 31, 256, 64), (128, 256, 0)):
+        assert lib.kat_gemm_bf16(P, P, None, P, m, n, k, None) == E.KAT_ERR_BAD_SHAPE
+        assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, m, n, k, 8, 0, None) == \
+            E.KAT_ERR_BAD_SHAPE
+        assert lib.kat_gemm_rational_bwd(P, P, P, P, P, P, P, P, P, 1 << 20, m, n, k, 8, 0,
+                                         None) == E.KAT_ERR_BAD_SHAPE
+        assert lib.kat_gemm_rational_bwd_workspace_bytes(m, n, 8, 0) == 0
+    assert lib.kat_gemm_bf16(None, P, None, P, 128, 256, 64, None) == E.KAT_ERR_NULL_POINTER
+    assert lib.kat_gemm_rational_fwd(P, P, None, None, P, P, P, 128, 256, 64, 8, 0, None) == \
+        E.KAT_ERR_NULL_POINTER
+    assert lib.kat_gemm_rational_bwd(P, P, P, P, P, P, None, P, P, 1 << 20, 128, 256, 64, 8, 0,
+                                     None) == E.KAT_ERR_NULL_POINTER
+    # groups: N / G must be a whole multiple of the 32-column epilogue chunk
+    for g in (0, -1, 3, 16):
+        assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, 128, 256, 64, g, 0, None) == \
+            E.KAT_ERR_BAD_GROUPS
+        assert lib.kat_gemm_rational_bwd(P, P, P, P, P, P, P, P, P, 1 << 20, 128, 256, 64, g, 0,
+                                         None) == E.KAT_ERR_BAD_GROUPS
+    for f in (-1, 2):
+        assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, 128, 256, 64, 8, f, None) == \
+            E.KAT_ERR_BAD_FORMULA
+    # TMA needs 16-byte aligned operands
+    assert lib.kat_gemm_bf16(P + 2, P, None, P, 128, 256, 64, None) == E.KAT_ERR_BAD_SHAPE
+    assert lib.kat_gemm_bf16(P, P, P + 8, P, 128, 256, 64, None) == E.KAT_ERR_BAD_SHAPE
+
+
 def _fwd(x=1, y=1, num=1, den=1, batch=4, channels=16, inner=1, groups=4, dtype=0):
     return _native.lib().kat_rational_fwd(x, y, num, den, batch, channels, inner, groups, dtype,
                                           None)
