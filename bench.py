@@ -81,6 +81,9 @@ def parse_args():
                     help="how the ViT step exchanges the KAT coefficient gradients")
     ap.add_argument("--vit-eager", action="store_true",
                     help="eager ViT steps on one GPU instead of the captured CUDA graph")
+    ap.add_argument("--vit-fused-gemm", action="store_true",
+                    help="ViT: KAN blocks run fc1 -> act2 -> fc2 on the tcgen05 GEMMs with act2 "
+                         "in their epilogues")
     ap.add_argument("--vit-compare", action="store_true",
                     help="also time the ViT step with the reference's PyTorch KAT formulation "
                          "and with plain GELU MLPs (one GPU)")
@@ -774,10 +777,10 @@ def run_vit(args):
     cfg = gv.vit_b16()
     B = args.vit_batch
 
-    def build(act="kat", kat_device="cuda"):
+    def build(act="kat", kat_device="cuda", fused_gemm=args.vit_fused_gemm):
         torch.manual_seed(0)
-        return gv.GRKANViT(dataclasses.replace(cfg, act=act), kat_device=kat_device).to(
-            dev, dtype=torch.bfloat16)
+        return gv.GRKANViT(dataclasses.replace(cfg, act=act, fused_gemm=fused_gemm),
+                           kat_device=kat_device).to(dev, dtype=torch.bfloat16)
 
     graphed = dist is None and not args.vit_eager
     model = build()
@@ -836,7 +839,9 @@ def run_vit(args):
         compare = {}
         del opt, graph_obj, step
         torch.cuda.empty_cache()
-        for name, kw in (("kat_torch_formulation", dict(kat_device="cpu")),
+        other = ("kat_unfused", dict(fused_gemm=False)) if args.vit_fused_gemm else \
+            ("kat_fused_gemm", dict(fused_gemm=True))
+        for name, kw in (other, ("kat_torch_formulation", dict(kat_device="cpu", fused_gemm=False)),
                          ("gelu_mlp", dict(act="gelu"))):
             m2 = build(**kw)
             o2 = gv.make_optimizer(m2, capturable=graphed)
@@ -850,6 +855,9 @@ def run_vit(args):
             "KAT_Group on the reference's PyTorch formulation (power stack + bmm, "
             "kat_1dgroup_torch.py) on the GPU, everything else identical")
         compare["gelu_mlp"]["what"] = "plain ViT-B/16 MLP (fc1 -> GELU -> fc2), no KAT"
+        compare[other[0]]["what"] = (
+            "KAN blocks on torch linears + KAT_Group kernels" if args.vit_fused_gemm else
+            "KAN blocks' fc1 -> act2 -> fc2 on the tcgen05 GEMMs with act2 in their epilogues")
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
@@ -872,6 +880,7 @@ def run_vit(args):
                 "global_batch": B * world, "per_gpu_batch": B, "image": [3, 224, 224],
                 "seq_len": cfg.num_tokens, "parallelism": f"dp{world}",
                 "kat_exchange": args.kat_exchange if world > 1 else None,
+                "fused_gemm": bool(args.vit_fused_gemm),
                 "optimizer": "AdamW (fused)", "params": "bf16",
                 "step": ("forward + loss + backward + optimizer captured in one CUDA graph"
                          if graphed else "eager" + (" with DistributedDataParallel over NCCL"
@@ -1086,6 +1095,222 @@ def run_bspline(args):
         dist.destroy_process_group()
 
 
+KAN_WORKLOAD = "kan_mlp_b16"
+KAN_METRIC = "GR-KAN MLP block (fc1 -> act2 -> fc2) fwd+bwd tokens/s"
+KAN_UNIT = "Mtokens/s"
+
+
+def _kan_block(C, H, G, dev, seed=0):
+    from rational_kat_cu_b200 import KAT_Group
+
+    torch.manual_seed(seed)
+    fc1 = torch.nn.Linear(C, H).to(dev, torch.bfloat16)
+    act2 = KAT_Group(num_groups=G, mode="gelu").to(dev)
+    fc2 = torch.nn.Linear(H, C).to(dev, torch.bfloat16)
+    return fc1, act2, fc2
+
+
+def _kan_cpu_rate(budget_s: float, steps: int = 0, warmup: int = 0):
+    """The reference's CPU path for the block: fp32 torch linears on the host cores with act2
+    evaluated by the oracle's restatement of kat_1dgroup_torch.py, forward + backward, on a
+    bounded number of tokens.  Returns (Mtokens/s, info)."""
+    from oracle import kat_torch_oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    C, H, G = 768, 3072, 8
+    torch.manual_seed(0)
+    fc1 = torch.nn.Linear(C, H)
+    fc2 = torch.nn.Linear(H, C)
+    from rational_kat_cu_b200 import KAT_Group
+    act = KAT_Group(num_groups=G, mode="gelu", device="cpu")
+    wn = act.weight_numerator.detach().clone().requires_grad_(True)
+    wd = act.weight_denominator.detach().clone().requires_grad_(True)
+
+    def run(tokens, n):
+        x = torch.randn(1, tokens, C, requires_grad=True)
+        gy = torch.randn(1, tokens, C)
+        t0 = time.perf_counter()
+        for _ in range(n):
+            h = fc1(x)
+            y = kat_torch_oracle.rational_1dgroup(h, wn.repeat(G, 1), wd, G)
+            fc2(y).backward(gy)
+        return (time.perf_counter() - t0) / max(n, 1)
+
+    per_token = run(197, 1) / 197
+    n_calls = (steps + warmup) if steps else 2
+    tokens = int(max(197, min(197 * 32, budget_s / max(n_calls, 1) / per_token)))
+    run(tokens, warmup if steps else 1)
+    reps = steps if steps else 1
+    dt = run(tokens, reps)
+    return tokens / dt / 1e6, {
+        "cores": cores, "tokens": tokens, "seconds_per_step": dt, "reps": reps,
+        "sample": f"fc1 -> act2 -> fc2 forward + backward on {tokens} tokens (768 -> 3072 -> "
+                  f"768), fp32 on the host cores, act2 by the oracle's kat_1dgroup_torch "
+                  f"restatement, mean of {reps} timed steps"}
+
+
+def run_kan_mlp_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    warm = max(0, min(args.warmup, 1))
+    rate, info = _kan_cpu_rate(args.cpu_seconds, steps=steps, warmup=warm)
+    print(json.dumps({
+        "impl": "reference", "metric": KAN_METRIC, "value": rate, "unit": KAN_UNIT,
+        "n_gpus": 0, "steps": steps, "warmup": warm, "ms_per_step": info["seconds_per_step"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": KAN_WORKLOAD, "tokens": info["tokens"]},
+        "cpu_baseline": {"value": rate, "unit": KAN_UNIT, "cores": info["cores"], "kind": "port",
+                         "sample": info["sample"]},
+        "e2e": {"value": rate, "unit": KAN_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_kan_mlp(args):
+    """Step = the GR-KAN ViT-B/16 MLP block fc1 (768 -> 3072) -> act2 (KAT 'gelu', 8 groups)
+    -> fc2 (3072 -> 768), forward + backward, on --vit-batch x 197 tokens of bf16, through
+    fused_gemm.kan_mlp_fused (act2 in the tcgen05 GEMM epilogues), captured in a CUDA graph.
+    The same block on cuBLAS linears + the activation kernels is timed beside it."""
+    import ctypes
+
+    from rational_kat_cu_b200 import fused_gemm
+
+    world, rank, local = dist_setup()
+    dist = init_process_group(world, rank, local) if world > 1 else None
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    C, H, G = 768, 3072, 8
+    M = args.vit_batch * 197
+    fc1, act2, fc2 = _kan_block(C, H, G, dev)
+    g = torch.Generator().manual_seed(rank)
+    x_h = torch.randn(M, C, generator=g).to(torch.bfloat16)
+    gy_h = (torch.randn(M, C, generator=g) * 0.05).to(torch.bfloat16)
+    x = x_h.to(dev).requires_grad_(True)
+    gy = gy_h.to(dev)
+    params = [*fc1.parameters(), *act2.parameters(), *fc2.parameters()]
+
+    def fused_step():
+        fused_gemm.kan_mlp_fused(x, fc1, act2, fc2).backward(gy)
+
+    def unfused_step():
+        fc2(act2(fc1(x))).backward(gy)
+
+    def graphed(fn):
+        for p in params + [x]:
+            p.grad = None
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        stream.wait_stream(side)
+        for p in params + [x]:
+            p.grad = None
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            fn()
+        return gr
+
+    g_fused = graphed(fused_step)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    ms = _time_steps(g_fused.replay, args.steps, args.warmup, dev, stream, dist)
+    g_unfused = graphed(unfused_step)
+    ms_unfused = _time_steps(g_unfused.replay, args.steps, args.warmup, dev, stream, dist)
+    del g_unfused
+
+    # the two fused kernels alone (C ABI through fused_gemm), graph-captured
+    num = act2.weight_numerator.detach().repeat(G, 1).contiguous()
+    den = act2.weight_denominator.detach().contiguous()
+    xd = x.detach()
+    w2t = fc2.weight.detach().t().contiguous()
+    h, _ = fused_gemm.gemm_rational_fwd(xd, fc1.weight, fc1.bias, num, den, G)
+
+    def kernel_ms(fn):
+        gr = torch.cuda.CUDAGraph()
+        fn()
+        with torch.cuda.graph(gr):
+            fn()
+        return _time_steps(gr.replay, max(5, args.kernel_iters // 4), 3, dev, stream)
+
+    f_ms = kernel_ms(lambda: fused_gemm.gemm_rational_fwd(xd, fc1.weight, fc1.bias, num, den, G))
+    b_ms = kernel_ms(lambda: fused_gemm.gemm_rational_bwd(gy, w2t, h, num, den, G))
+    p_ms = kernel_ms(lambda: fused_gemm.gemm_bf16(xd, fc1.weight, fc1.bias))
+    c_ms = kernel_ms(lambda: torch.nn.functional.linear(xd, fc1.weight, fc1.bias))
+
+    # e2e through the module API: x and the output gradient uploaded from pinned host memory,
+    # dx read back into pinned host memory, every step (eager)
+    hx, hgy = x_h.pin_memory(), gy_h.pin_memory()
+    hdx = torch.empty(M, C, dtype=torch.bfloat16, pin_memory=True)
+
+    def e2e_step():
+        xi = hx.to(dev, non_blocking=True).requires_grad_(True)
+        fused_gemm.kan_mlp_fused(xi, fc1, act2, fc2).backward(hgy.to(dev, non_blocking=True))
+        hdx.copy_(xi.grad, non_blocking=True)
+
+    e_ms = _time_steps(e2e_step, max(3, args.e2e_steps), 2, dev, stream, dist)
+    status = fused_gemm.device_status(local)
+    clocks = None
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary()
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        rate, info = _kan_cpu_rate(budget_s=args.cpu_seconds)
+        cpu = {"value": rate, "unit": KAN_UNIT, "cores": info["cores"], "kind": "port",
+               "sample": info["sample"]}
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        flops_gemm = 2.0 * M * H * C
+        peak_tf = _bf16_peak()
+        print(json.dumps({
+            "metric": KAN_METRIC, "value": world * M / (ms * 1e-3) / 1e6, "unit": KAN_UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": KAN_WORKLOAD, "tokens_per_gpu": M, "in_features": C,
+                       "hidden": H, "groups": G, "step": "forward + backward in one CUDA graph",
+                       "l2": "activations of one step (155 MB per [tokens, 3072] tensor) exceed L2"},
+            "roofline": {"bound": "tensor", "kernel": "kat_gemm_kernel<1, 0> (fc1 + act2 forward)",
+                         "achieved": flops_gemm / (f_ms * 1e-3) / 1e12, "peak": peak_tf[0],
+                         "unit": "TFLOP/s", "frac": flops_gemm / (f_ms * 1e-3) / 1e12 / peak_tf[0],
+                         "peak_source": peak_tf[1], "traffic": None,
+                         "algorithmic_flops_per_launch": flops_gemm, "ms_per_launch": f_ms},
+            "kernels": {"fused_fwd_ms": f_ms, "fused_bwd_ms": b_ms, "plain_gemm_ms": p_ms,
+                        "cublas_fc1_ms": c_ms,
+                        "plain_gemm_tflops": flops_gemm / (p_ms * 1e-3) / 1e12,
+                        "cublas_fc1_tflops": flops_gemm / (c_ms * 1e-3) / 1e12},
+            "compare": {"unfused_ms_per_step": ms_unfused,
+                        "unfused_value": world * M / (ms_unfused * 1e-3) / 1e6,
+                        "what": "same block on torch linears (cuBLAS) + KAT_Group kernels"},
+            "e2e": {"value": world * M / (e_ms * 1e-3) / 1e6, "unit": KAN_UNIT,
+                    "h2d_bytes_per_step": world * M * C * 2 * 2,
+                    "d2h_bytes_per_step": world * M * C * 2, "ms_per_step": e_ms,
+                    "api": "fused_gemm.kan_mlp_fused forward + backward, pinned host x / grad in, "
+                           "dx out"},
+            "gpu_launches": 4 * args.steps * world,
+            "device_status": status,
+            "cpu_baseline": cpu, "clocks": clocks,
+        }), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _bf16_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured bf16_tflops (burst)"
+    except Exception:
+        return 1590.0, "fallback bf16 TFLOP/s (burst)"
+
+
 def main():
     args = parse_args()
     if args.workload == BSPLINE_WORKLOAD:
@@ -1098,6 +1323,11 @@ def main():
             run_vit_reference(args)
         else:
             run_vit(args)
+    elif args.workload == KAN_WORKLOAD:
+        if args.impl == "reference":
+            run_kan_mlp_reference(args)
+        else:
+            run_kan_mlp(args)
     elif args.impl == "reference":
         run_reference(args)
     elif args.sweep:

@@ -1,7 +1,7 @@
 // kat_gemm.cu — sm_100a tensor-core GEMM (C = A B^T, bf16 in, fp32 accumulate) with the
 // group-rational activation fused into its epilogue (C ABI: include/kat_gemm.h).
 //
-// One persistent CTA per SM, 192 threads in three roles:
+// One persistent CTA per SM, 576 threads in three roles:
 //   warp 0, one lane   TMA producer: per k-block, a 128 x 64 tile of A and a 256 x 64 tile of B
 //                      (bf16, 128-byte swizzled rows) into a ring of shared-memory stages;
 //   warp 1, one lane   MMA issuer: tcgen05.mma (kind::f16, M = 128, N = 256, K = 16) from the
@@ -9,19 +9,24 @@
 //                      accumulators in tensor memory; tcgen05.commit frees the stage when its
 //                      MMAs have read it and, after the last k-block, hands the accumulator to
 //                      the epilogue.  Warp 1 also allocates and frees the 512 TMEM columns;
-//   warps 2-5          epilogue: thread r of the 128 owns accumulator row r (TMEM lane r; a
-//                      warp may read only its lane quadrant, warp % 4), reads 32 columns at a
-//                      time with tcgen05.ld, applies the epilogue, writes the bf16 results into
-//                      a 64-byte-swizzled staging tile and one thread stores the tile with TMA.
+//   warps 2-17         epilogue, 16 independent warps: warp w owns the 32 accumulator rows of
+//                      its TMEM lane quadrant (a warp may read only lanes 32 (w % 4) .. + 31)
+//                      and one 64-column slice of the tile, which it reads 16 columns at a time
+//                      with tcgen05.ld, runs through the epilogue, writes as bf16 into its own
+//                      64-byte-swizzled 32 x 32 staging tile and stores with TMA (lane 0).  Four
+//                      epilogue warps per SM sub-partition keep the FP32 pipe busy while the
+//                      tensor pipe runs the next tile.
 // With two accumulators the epilogue of one output tile overlaps the mainloop of the next.
-// Tiles are numbered row-block-major (12 consecutive tiles share a 128-row block of A) and
-// CTA c takes tiles c, c + grid, c + 2 grid, ...
+// Tiles are numbered column-block-major (consecutive tiles share a 256-column block of B, so a
+// CTA's tiles c, c + grid, c + 2 grid, ... mostly stay in one block of channel groups); A and
+// B are re-read from L2.
 //
 // Epilogues: plain (C = bf16(acc + bias)); forward (h = bf16(acc + bias), y = rational(h) with
 // the activation kernels' per-element math, so y is bit-identical to kat_rational_fwd on h);
-// backward (g = bf16(acc), h streamed in by TMA, dh = the activation kernels' per-element
-// backward on (h, g), per-thread fp32 gradient sums flushed in a fixed order into per-warp fp64
-// partials, then a second kernel adds the partials of all warps in a fixed order).
+// backward (g = bf16(acc), the warp's 32 x 32 tile of h loaded by TMA one chunk ahead, dh = the
+// activation kernels' per-element backward on (h, g), per-thread fp32 gradient sums flushed in
+// a fixed order into per-warp fp64 partials, then a second kernel adds the partials of all
+// warps in a fixed order).
 //
 // Every mbarrier wait is bounded (about two seconds of clock cycles).  A wait that runs out
 // sets the CTA's abort flag and the sticky device status word; the other roles see the flag
@@ -48,42 +53,53 @@ constexpr int kBM = 128;       // tile rows (MMA M, TMEM lanes)
 constexpr int kBN = 256;       // tile columns (MMA N, TMEM columns per accumulator)
 constexpr int kBK = 64;        // k-block: 64 bf16 = one 128-byte swizzle row
 constexpr int kUmmaK = 16;     // K of one kind::f16 MMA
-constexpr int kChunk = 32;     // epilogue columns per tcgen05.ld
-constexpr int kChunks = kBN / kChunk;
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
 constexpr int kEpiWarp0 = 2;
+constexpr int kMaxEpiWarps = 16;
+constexpr int kChunk = 32;                     // columns per staging tile / TMA store
+constexpr int kHalf = 16;                      // columns per tcgen05.ld
+constexpr int kWarpRows = 32;
 constexpr uint32_t kTmemCols = 2 * kBN;
 constexpr uint32_t kABytes = kBM * kBK * 2;
 constexpr uint32_t kBBytes = kBN * kBK * 2;
-constexpr uint32_t kChunkBytes = kBM * kChunk * 2;  // 128 rows x 64 bytes
-constexpr int kHBufs = 4;                          // backward: h chunks in flight
-constexpr uint32_t kBarBytes = 256;
+constexpr uint32_t kTileBytes = kWarpRows * kChunk * 2;  // 32 rows x 64 bytes
+constexpr uint32_t kBarBytes = 512;
 constexpr long long kWaitCycles = 4000000000LL;
 constexpr int kStatusWaitTimeout = KAT_DEVICE_WAIT_TIMEOUT;
 
 enum Mode { kPlain = 0, kFwd = 1, kBwd = 2 };
 
+// Per mode: mainloop stages, epilogue warps (a multiple of 4: one per TMEM lane quadrant and
+// column slice), staging tiles per epilogue warp (outputs) and h tiles per epilogue warp.  The
+// light plain / forward epilogues keep up with 8 warps and leave shared memory for 4 stages; the
+// FP32-heavy backward epilogue gets 16 warps (4 per SM sub-partition).
 template <int kMode> struct Cfg;
 template <> struct Cfg<kPlain> {
-  static constexpr int kStages = 4, kOuts = 1, kH = 0;
+  static constexpr int kStages = 4, kEpiWarps = 8, kOuts = 1, kH = 0;
 };
 template <> struct Cfg<kFwd> {
-  static constexpr int kStages = 4, kOuts = 2, kH = 0;
+  static constexpr int kStages = 4, kEpiWarps = 8, kOuts = 2, kH = 0;
 };
 template <> struct Cfg<kBwd> {
-  static constexpr int kStages = 3, kOuts = 1, kH = kHBufs;
+  static constexpr int kStages = 3, kEpiWarps = 16, kOuts = 1, kH = 1;
 };
+
+template <int kMode>
+constexpr int threads_of() {
+  return (kEpiWarp0 + Cfg<kMode>::kEpiWarps) * 32;
+}
 
 template <int kMode>
 constexpr uint32_t smem_bytes() {
   return 1024 + Cfg<kMode>::kStages * (kABytes + kBBytes) +
-         2 * Cfg<kMode>::kOuts * kChunkBytes + Cfg<kMode>::kH * kChunkBytes + kBarBytes;
+         Cfg<kMode>::kEpiWarps * (Cfg<kMode>::kOuts + Cfg<kMode>::kH) * kTileBytes + kBarBytes;
 }
+static_assert(smem_bytes<kPlain>() <= 227 * 1024, "plain shared memory");
 static_assert(smem_bytes<kFwd>() <= 227 * 1024, "forward shared memory");
 static_assert(smem_bytes<kBwd>() <= 227 * 1024, "backward shared memory");
 
 struct GemmArgs {
+  int32_t m;            // rows of A and of the outputs
+  int32_t m_tiles;      // row tiles (ceil(M / 128))
   int32_t n_tiles;      // column tiles (N / 256)
   int32_t num_tiles;    // row tiles x column tiles
   int32_t k_blocks;     // K / 64
@@ -92,7 +108,7 @@ struct GemmArgs {
   const uint16_t* bias;   // bf16 [N] or null
   const float* num;       // [G, 6]
   const float* den;       // [G, 4]
-  double* partial;        // backward: [grid][4][G][10]
+  double* partial;        // backward: [grid][16 warps][G][10]; row 0 of a CTA ends as its sum
 };
 
 __device__ int g_gemm_status;
@@ -127,12 +143,26 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
+// try_wait that lets the thread sleep in hardware until the phase completes or about
+// kSuspendNs have passed, so a waiting thread takes no issue slots from the busy warps.
+constexpr uint32_t kSuspendNs = 20000;
+__device__ __forceinline__ bool mbar_try_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return done != 0;
+}
 // Bounded wait of one thread for the phase with `parity`; false when the CTA aborted or this
 // wait ran out (which aborts the CTA).
 __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try(bar, parity)) {
+  while (!mbar_try_suspend(bar, parity)) {
     if (*abort) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort = 1;
@@ -170,9 +200,6 @@ __device__ __forceinline__ void bulk_wait_all() {
 }
 __device__ __forceinline__ void fence_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void epi_bar() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
 }
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -212,21 +239,27 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
           smem_u32(bar))
       : "memory");
 }
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+// 16 consecutive fp32 columns of this thread's TMEM lane; the values are valid after
+// tmem_wait on the same registers.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32"
-      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
-      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
         "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
-        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
-        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
-        "=r"(v[31])
+        "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Wait for this thread's outstanding tcgen05.ld; the registers are tied to the wait so no use
+// of them is scheduled before it.
+__device__ __forceinline__ void tmem_wait(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                 "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                 "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
 }
 
 // Shared-memory matrix descriptor of a K-major bf16 tile with 128-byte rows, 128-byte swizzle,
@@ -257,30 +290,32 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) {
 // ---------------------------------------------------------------------------
 
 template <int kMode, int kF>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_of<kMode>(), 1)
 kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_out0,
                 const __grid_constant__ CUtensorMap tm_out1,
                 const __grid_constant__ CUtensorMap tm_h, const GemmArgs args) {
   constexpr int S = Cfg<kMode>::kStages;
   constexpr int kOuts = Cfg<kMode>::kOuts;
+  constexpr int kEpiWarps = Cfg<kMode>::kEpiWarps;
+  constexpr int kSlice = kBN / (kEpiWarps / 4);  // columns per epilogue warp and tile
+  constexpr int kChunksPerSlice = kSlice / kChunk;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = s_a + S * kABytes;
-  uint8_t* s_out = s_b + S * kBBytes;                    // [2 buffers][kOuts] chunk tiles
-  uint8_t* s_h = s_out + 2 * kOuts * kChunkBytes;        // backward: [kHBufs] chunk tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + Cfg<kMode>::kH * kChunkBytes);
+  uint8_t* s_out = s_b + S * kBBytes;                  // [epilogue warp][kOuts] 32 x 32 tiles
+  uint8_t* s_h = s_out + kEpiWarps * kOuts * kTileBytes;  // backward: [epilogue warp] h tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + kEpiWarps * Cfg<kMode>::kH * kTileBytes);
   uint64_t* full = bars;              // [S]  TMA -> MMA
   uint64_t* empty = full + S;         // [S]  MMA -> TMA
   uint64_t* tfull = empty + S;        // [2]  MMA -> epilogue
-  uint64_t* tempty = tfull + 2;       // [2]  epilogue -> MMA
-  uint64_t* hbar = tempty + 2;        // [kHBufs] backward h loads
-  uint64_t* drain = hbar + kHBufs;    // MMA completion before teardown
+  uint64_t* tempty = tfull + 2;       // [2]  epilogue warps -> MMA
+  uint64_t* hbar = tempty + 2;        // [kEpiWarps] backward h loads
+  uint64_t* drain = hbar + kEpiWarps; // MMA completion before teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* epi_ok = abort + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -292,12 +327,11 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(tfull + j, 1);
-      mbar_init(tempty + j, kEpiThreads);
+      mbar_init(tempty + j, kEpiWarps);
     }
-    for (int j = 0; j < kHBufs; ++j) mbar_init(hbar + j, 1);
+    for (int j = 0; j < kEpiWarps; ++j) mbar_init(hbar + j, 1);
     mbar_init(drain, 1);
     *abort = 0;
-    *epi_ok = 1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_map(&tm_a);
     prefetch_map(&tm_b);
@@ -311,7 +345,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int n_tiles = args.n_tiles;
+  const int m_tiles = args.m_tiles;
   const int num_tiles = args.num_tiles;
   const int k_blocks = args.k_blocks;
 
@@ -321,8 +355,8 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * kBM;
-        const int n0 = (tile % n_tiles) * kBN;
+        const int m0 = (tile % m_tiles) * kBM;
+        const int n0 = (tile / m_tiles) * kBN;
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!wait_phase(empty + stage, phase ^ 1u, abort)) { ok = false; break; }
@@ -380,34 +414,40 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
       }
     }
   } else {
-    // ---------------- epilogue ----------------
-    const int quad = warp & 3;                 // TMEM lane quadrant this warp may access
-    const int row = quad * 32 + lane;          // accumulator row within the tile
-    const int et = threadIdx.x - kEpiWarp0 * 32;
+    // ---------------- epilogue (independent warps) ----------------
+    const int ew = warp - kEpiWarp0;              // 0 .. kEpiWarps - 1
+    const int quad = warp & 3;                    // TMEM lane quadrant this warp may access
+    const int slice = ew >> 2;                    // 64-column slice of the tile
+    const int row = lane;                         // row within the warp's 32-row tile
     const uint32_t lane_addr = tmem_base + (uint32_t(quad * 32) << 16);
-    const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const int total_chunks = my_tiles * kChunks;
+    const int my_tiles = (num_tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1;
+    const int total_chunks = my_tiles * kChunksPerSlice;
+    uint8_t* stage_out = s_out + ew * kOuts * kTileBytes;
+    uint8_t* stage_h = s_h + ew * kTileBytes;
+    uint64_t* my_hbar = hbar + ew;
 
     double* wpart = nullptr;
     if constexpr (kMode == kBwd) {
-      wpart = args.partial + (size_t(blockIdx.x) * 4 + (warp - kEpiWarp0)) * size_t(args.groups) * kAcc;
+      wpart = args.partial + (size_t(blockIdx.x) * kEpiWarps + ew) * size_t(args.groups) * kAcc;
       for (int i = lane; i < args.groups * kAcc; i += 32) wpart[i] = 0.0;
       __syncwarp();
     }
-    // h chunk q lives at tile blockIdx.x + (q / kChunks) * grid, columns (q % kChunks) * 32.
+    // Chunk q of this warp: tile blockIdx.x + (q / chunks per slice) * grid, columns
+    // slice * kSlice + (q % chunks per slice) * 32, rows quad * 32 .. + 31 of that tile.
+    auto chunk_origin = [&](int q, int& m0, int& n0) {
+      const int tile = blockIdx.x + (q / kChunksPerSlice) * gridDim.x;
+      m0 = (tile % m_tiles) * kBM + quad * kWarpRows;
+      n0 = (tile / m_tiles) * kBN + slice * kSlice + (q % kChunksPerSlice) * kChunk;
+    };
     auto issue_h = [&](int q) {
       if constexpr (kMode == kBwd) {
-        const int tile = blockIdx.x + (q / kChunks) * gridDim.x;
-        const int m0 = (tile / n_tiles) * kBM;
-        const int n0 = (tile % n_tiles) * kBN + (q % kChunks) * kChunk;
-        uint64_t* bar = hbar + (q % kHBufs);
-        mbar_expect_tx(bar, kChunkBytes);
-        tma_load_2d(s_h + (q % kHBufs) * kChunkBytes, &tm_h, bar, n0, m0);
+        int m0, n0;
+        chunk_origin(q, m0, n0);
+        mbar_expect_tx(my_hbar, kTileBytes);
+        tma_load_2d(stage_h, &tm_h, my_hbar, n0, m0);
       }
     };
-    if (kMode == kBwd && et == 0) {
-      for (int q = 0; q < kHBufs && q < total_chunks; ++q) issue_h(q);
-    }
+    if (kMode == kBwd && lane == 0 && total_chunks > 0) issue_h(0);
 
     FwdCoef<float2> fc;
     BwdCoef<float2> bc;
@@ -433,6 +473,14 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
         if (lane == k) mine = tot[k];
       if (lane < kAcc) wpart[size_t(g) * kAcc + lane] += mine;
     };
+    // Lane 0 waits (bounded); the warp leaves together on the broadcast outcome.
+    auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      int ok = 1;
+      if (lane == 0) ok = wait_phase(bar, parity, abort) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (ok) (void)mbar_try(bar, parity);  // completed: acquire for every lane
+      return ok != 0;
+    };
 
     int q = 0;
     int local = 0;
@@ -440,137 +488,152 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      const int m0 = (tile / n_tiles) * kBM;
-      const int tile_n0 = (tile % n_tiles) * kBN;
-      for (int c = 0; c < kChunks; ++c, ++q) {
-        const int n0 = tile_n0 + c * kChunk;
-        const int buf = q & 1;
-        // One thread waits (bounded) for what this chunk needs; the barrier below publishes
-        // the outcome so the 128 threads leave together.
-        if (et == 0) {
-          bool ok = true;
-          if (c == 0) ok = wait_phase(tfull + acc, acc_phase, abort);
-          if (kMode == kBwd && ok) ok = wait_phase(hbar + (q % kHBufs), (q / kHBufs) & 1, abort);
-          bulk_wait_read<1>();  // staging buffer `buf` (used two chunks ago) has been read
-          *epi_ok = ok ? 1 : 0;
-        }
-        epi_bar();
-        if (!*epi_ok) { alive = false; break; }
-        if (c == 0) {
-          (void)mbar_try(tfull + acc, acc_phase);  // completed: acquire for this thread
-          tc_fence_after();
-        }
-        uint32_t v[32];
-        tmem_ld32(lane_addr + uint32_t(acc * kBN + c * kChunk), v);
-        if (c == kChunks - 1) {
-          tc_fence_before();
-          mbar_arrive(tempty + acc);
-        }
-        uint8_t* stage0 = s_out + (buf * kOuts) * kChunkBytes;
-        uint32_t w0[16];
-        uint32_t w1[16];
-        if constexpr (kMode == kPlain || kMode == kFwd) {
-          float bias[32];
-          if (args.bias != nullptr) {
-            const uint4* bp = reinterpret_cast<const uint4*>(args.bias + n0);
+      if (!warp_wait(tfull + acc, acc_phase)) break;
+      tc_fence_after();
+      for (int c = 0; c < kChunksPerSlice; ++c, ++q) {
+        int m0, n0;
+        chunk_origin(q, m0, n0);
+        const int g = n0 / args.group_width;
+        uint32_t hw[16];
+        if constexpr (kMode == kBwd) {
+          if (!warp_wait(my_hbar, uint32_t(q & 1))) { alive = false; break; }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 u = __ldg(bp + j);
-              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                bias[j * 8 + t * 2] = bf16_bits_to_float(uw[t] & 0xFFFFu);
-                bias[j * 8 + t * 2 + 1] = bf16_bits_to_float(uw[t] >> 16);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) bias[j] = 0.0f;
+          for (int j = 0; j < 4; ++j) {
+            const uint4 u = *reinterpret_cast<const uint4*>(stage_h + sw64_offset(row, j));
+            hw[j * 4 + 0] = u.x; hw[j * 4 + 1] = u.y; hw[j * 4 + 2] = u.z; hw[j * 4 + 3] = u.w;
           }
-          if constexpr (kMode == kFwd) {
-            const int g = n0 / args.group_width;
-            if (g != cur_group) {
-              cur_group = g;
-              load_fwd_coef<float2, kF>(args.num, args.den, g, fc);
-            }
-          }
-#pragma unroll
-          for (int p = 0; p < 16; ++p) {
-            const float2 hv = make_float2(__fadd_rn(__uint_as_float(v[2 * p]), bias[2 * p]),
-                                          __fadd_rn(__uint_as_float(v[2 * p + 1]), bias[2 * p + 1]));
-            w0[p] = Codec<__nv_bfloat16>::pack_word(hv);
-            if constexpr (kMode == kFwd) {
-              const float2 hx = Codec<__nv_bfloat16>::unpack_word(w0[p]);
-              w1[p] = Codec<__nv_bfloat16>::pack_word(fwd_math<float2, false, kF>(hx, fc));
-            }
-          }
-        } else {
-          const int g = n0 / args.group_width;
+          __syncwarp();  // the h tile is in registers: load the next chunk's into it
+          if (lane == 0 && q + 1 < total_chunks) issue_h(q + 1);
           if (g != cur_group) {
             if (cur_group >= 0) flush(cur_group);
             cur_group = g;
             load_bwd_coef<float2, kF>(args.num, args.den, g, bc);
           }
-          (void)mbar_try(hbar + (q % kHBufs), (q / kHBufs) & 1);  // completed: acquire
-          const uint8_t* hrow = s_h + (q % kHBufs) * kChunkBytes;
-          uint32_t hw[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 u = *reinterpret_cast<const uint4*>(hrow + sw64_offset(row, j));
-            hw[j * 4 + 0] = u.x; hw[j * 4 + 1] = u.y; hw[j * 4 + 2] = u.z; hw[j * 4 + 3] = u.w;
-          }
-#pragma unroll
-          for (int p = 0; p < 16; ++p) {
-            const uint32_t gw = Codec<__nv_bfloat16>::pack_word(
-                make_float2(__uint_as_float(v[2 * p]), __uint_as_float(v[2 * p + 1])));
-            const float2 go = Codec<__nv_bfloat16>::unpack_word(gw);
-            const float2 x = Codec<__nv_bfloat16>::unpack_word(hw[p]);
-            w0[p] = Codec<__nv_bfloat16>::pack_word(bwd_math<float2, false, kF>(x, go, bc, acc_g));
+        } else if constexpr (kMode == kFwd) {
+          if (g != cur_group) {
+            cur_group = g;
+            load_fwd_coef<float2, kF>(args.num, args.den, g, fc);
           }
         }
-        // Staging tile(s), 64-byte swizzled rows, then one TMA store per output.
+        // One 16-column half: epilogue math on v, bf16 words into the staging tile(s).
+        auto do_half = [&](uint32_t (&v)[16], const int half) {
+          uint32_t w0[8];
+          uint32_t w1[8];
+          if constexpr (kMode == kPlain || kMode == kFwd) {
+            float bias[16];
+            if (args.bias != nullptr) {
+              const uint4* bp = reinterpret_cast<const uint4*>(args.bias + n0 + half * kHalf);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(stage0 + sw64_offset(row, j)) =
-              make_uint4(w0[j * 4], w0[j * 4 + 1], w0[j * 4 + 2], w0[j * 4 + 3]);
-        if constexpr (kMode == kFwd) {
-          uint8_t* stage1 = stage0 + kChunkBytes;
+              for (int j = 0; j < 2; ++j) {
+                const uint4 u = __ldg(bp + j);
+                const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(stage1 + sw64_offset(row, j)) =
-                make_uint4(w1[j * 4], w1[j * 4 + 1], w1[j * 4 + 2], w1[j * 4 + 3]);
+                for (int t = 0; t < 4; ++t) {
+                  bias[j * 8 + t * 2] = bf16_bits_to_float(uw[t] & 0xFFFFu);
+                  bias[j * 8 + t * 2 + 1] = bf16_bits_to_float(uw[t] >> 16);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) bias[j] = 0.0f;
+            }
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+              const float2 hv =
+                  make_float2(__fadd_rn(__uint_as_float(v[2 * p]), bias[2 * p]),
+                              __fadd_rn(__uint_as_float(v[2 * p + 1]), bias[2 * p + 1]));
+              w0[p] = Codec<__nv_bfloat16>::pack_word(hv);
+              if constexpr (kMode == kFwd) {
+                const float2 hx = Codec<__nv_bfloat16>::unpack_word(w0[p]);
+                w1[p] = Codec<__nv_bfloat16>::pack_word(fwd_math<float2, false, kF>(hx, fc));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int p = 0; p < 8; ++p) {
+              const uint32_t gw = Codec<__nv_bfloat16>::pack_word(
+                  make_float2(__uint_as_float(v[2 * p]), __uint_as_float(v[2 * p + 1])));
+              const float2 go = Codec<__nv_bfloat16>::unpack_word(gw);
+              const float2 x = Codec<__nv_bfloat16>::unpack_word(hw[half * 8 + p]);
+              w0[p] = Codec<__nv_bfloat16>::pack_word(bwd_math<float2, false, kF>(x, go, bc, acc_g));
+            }
+          }
+          if (half == 0) {
+            // the staging tile's previous TMA store has finished reading it
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            *reinterpret_cast<uint4*>(stage_out + sw64_offset(row, half * 2 + j)) =
+                make_uint4(w0[j * 4], w0[j * 4 + 1], w0[j * 4 + 2], w0[j * 4 + 3]);
+          if constexpr (kMode == kFwd) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              *reinterpret_cast<uint4*>(stage_out + kTileBytes + sw64_offset(row, half * 2 + j)) =
+                  make_uint4(w1[j * 4], w1[j * 4 + 1], w1[j * 4 + 2], w1[j * 4 + 3]);
+          }
+        };
+        // The second half's TMEM load is in flight while the first half is computed.
+        const uint32_t col = uint32_t(acc * kBN + slice * kSlice + c * kChunk);
+        uint32_t va[16];
+        uint32_t vb[16];
+        tmem_ld16(lane_addr + col, va);
+        tmem_wait(va);
+        tmem_ld16(lane_addr + col + kHalf, vb);
+        do_half(va, 0);
+        tmem_wait(vb);
+        if (c == kChunksPerSlice - 1) {
+          // this warp has read its part of the accumulator: hand it back to the MMA issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty + acc);
         }
+        do_half(vb, 1);
         fence_async_shared();
-        epi_bar();
-        if (et == 0) {
-          tma_store_2d(&tm_out0, stage0, n0, m0);
-          if constexpr (kMode == kFwd) tma_store_2d(&tm_out1, stage0 + kChunkBytes, n0, m0);
+        __syncwarp();
+        if (lane == 0 && m0 < args.m) {  // rows past M: nothing to store (tail tile)
+          tma_store_2d(&tm_out0, stage_out, n0, m0);
+          if constexpr (kMode == kFwd) tma_store_2d(&tm_out1, stage_out + kTileBytes, n0, m0);
           bulk_commit();
-          if (kMode == kBwd && q + kHBufs < total_chunks) issue_h(q + kHBufs);
         }
       }
     }
     if constexpr (kMode == kBwd) {
       if (alive && cur_group >= 0) flush(cur_group);
     }
-    if (et == 0) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   }
 
+  tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
     tmem_free(tmem_base, kTmemCols);
   }
+  if constexpr (kMode == kBwd) {
+    // This CTA's warp rows, added in warp order into its row 0 (the reduction kernel then
+    // reads one row per CTA).  The partial rows were written before the barrier above.
+    if (threadIdx.x >= kEpiWarp0 * 32) {
+      double* base = args.partial + size_t(blockIdx.x) * kEpiWarps * size_t(args.groups) * kAcc;
+      const int n = args.groups * kAcc;
+      for (int i = threadIdx.x - kEpiWarp0 * 32; i < n; i += kEpiWarps * 32) {
+        double t = 0.0;
+        for (int w = 0; w < kEpiWarps; ++w) t += base[size_t(w) * n + i];
+        base[i] = t;
+      }
+    }
+  }
 }
 
-// Coefficient gradients: one warp per group adds the partial rows of every (CTA, epilogue
-// warp) in a fixed order (lane-strided, then a fixed shuffle tree) and writes d_num / d_den
-// with the sign conventions of the activation kernels.
+// Coefficient gradients: one warp per group adds the CTA rows (row 0 of each CTA's block of
+// row_stride warp rows) in a fixed order (lane-strided, then a fixed shuffle tree) and writes
+// d_num / d_den with the sign conventions of the activation kernels.
 constexpr int kReduceWarps = 8;
 __global__ void __launch_bounds__(kReduceWarps * 32)
-kat_gemm_reduce_kernel(const double* __restrict__ partial, int rows, int groups,
-                       const float* __restrict__ den, float* __restrict__ d_num,
+kat_gemm_reduce_kernel(const double* __restrict__ partial, int rows, int row_stride,
+                       int groups, const float* __restrict__ den, float* __restrict__ d_num,
                        float* __restrict__ d_den, int formula) {
   const int g = blockIdx.x * kReduceWarps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -579,7 +642,7 @@ kat_gemm_reduce_kernel(const double* __restrict__ partial, int rows, int groups,
 #pragma unroll
   for (int k = 0; k < kAcc; ++k) tot[k] = 0.0;
   for (int r = lane; r < rows; r += 32) {
-    const double* src = partial + (size_t(r) * groups + g) * kAcc;
+    const double* src = partial + (size_t(r) * row_stride * groups + g) * kAcc;
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
   }
@@ -690,7 +753,7 @@ int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o0,
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
       cudaSuccess)
     return KAT_ERR_CUDA;
-  kernel<<<grid, kThreads, smem, stream>>>(a, b, o0, o1, h, args);
+  kernel<<<grid, threads_of<kMode>(), smem, stream>>>(a, b, o0, o1, h, args);
   return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
 
@@ -717,9 +780,11 @@ int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c, int64
   CUtensorMap ma, mb, mc;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mc, c, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+      !make_map(&mc, c, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
+  args.m = int32_t(m);
+  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
   args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
@@ -749,10 +814,12 @@ int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const 
   CUtensorMap ma, mb, mh, my;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mh, h, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !make_map(&my, y, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+      !make_map(&mh, h, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&my, y, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
+  args.m = int32_t(m);
+  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
   args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
@@ -772,7 +839,7 @@ size_t kat_gemm_rational_bwd_workspace_bytes(int64_t m, int64_t n, int32_t num_g
   if (check_shape(m, n, kBK) != KAT_OK || num_groups < 1) return 0;
   const int grid = grid_for(m, n, device);
   if (grid <= 0) return 0;
-  return size_t(grid) * 4 * size_t(num_groups) * kAcc * sizeof(double);
+  return size_t(grid) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
 }
 
 int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const float* num,
@@ -790,16 +857,18 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   if (int st = current_device(&dev)) return st;
   const int grid = grid_for(m, n, dev);
   if (grid <= 0) return KAT_ERR_CUDA;
-  const size_t need = size_t(grid) * 4 * size_t(num_groups) * kAcc * sizeof(double);
+  const size_t need = size_t(grid) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return KAT_ERR_WORKSPACE;
   CUtensorMap ma, mb, mh, md;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mh, h, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !make_map(&md, dh, m, n, kChunk, kBM, CU_TENSOR_MAP_SWIZZLE_64B))
+      !make_map(&mh, h, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&md, dh, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
+  args.m = int32_t(m);
+  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
   args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
@@ -815,7 +884,7 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   if (rc != KAT_OK) return rc;
   const int rgrid = (num_groups + kReduceWarps - 1) / kReduceWarps;
   kat_gemm_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, st>>>(
-      static_cast<const double*>(workspace), grid * 4, num_groups, den, d_num, d_den, formula);
+      static_cast<const double*>(workspace), grid, Cfg<kBwd>::kEpiWarps, num_groups, den, d_num, d_den, formula);
   return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
 
