@@ -38,6 +38,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -60,7 +61,6 @@ constexpr int kHalf = 16;                      // columns per tcgen05.ld
 constexpr int kWarpRows = 32;
 constexpr uint32_t kTmemCols = 2 * kBN;
 constexpr uint32_t kABytes = kBM * kBK * 2;
-constexpr uint32_t kBBytes = kBN * kBK * 2;
 constexpr uint32_t kTileBytes = kWarpRows * kChunk * 2;  // 32 rows x 64 bytes
 constexpr uint32_t kBarBytes = 512;
 constexpr long long kWaitCycles = 4000000000LL;
@@ -68,38 +68,51 @@ constexpr int kStatusWaitTimeout = KAT_DEVICE_WAIT_TIMEOUT;
 
 enum Mode { kPlain = 0, kFwd = 1, kBwd = 2 };
 
-// Per mode: mainloop stages, epilogue warps (a multiple of 4: one per TMEM lane quadrant and
-// column slice), staging tiles per epilogue warp (outputs) and h tiles per epilogue warp.  The
-// light plain / forward epilogues keep up with 8 warps and leave shared memory for 4 stages; the
-// FP32-heavy backward epilogue gets 16 warps (4 per SM sub-partition).
+// Per mode: mainloop stages (one CTA per tile / two CTAs per 256-row tile), epilogue warps (a
+// multiple of 4: one per TMEM lane quadrant and column slice), staging tiles per epilogue warp
+// (outputs) and h tiles per epilogue warp.  The light plain / forward epilogues keep up with 8
+// warps; the FP32-heavy backward epilogue gets 16 warps (4 per SM sub-partition).
 template <int kMode> struct Cfg;
 template <> struct Cfg<kPlain> {
-  static constexpr int kStages = 4, kEpiWarps = 8, kOuts = 1, kH = 0;
+  static constexpr int kStages1 = 4, kStages2 = 6, kEpiWarps = 8, kOuts = 1, kH = 0;
 };
 template <> struct Cfg<kFwd> {
-  static constexpr int kStages = 4, kEpiWarps = 8, kOuts = 2, kH = 0;
+  static constexpr int kStages1 = 4, kStages2 = 6, kEpiWarps = 8, kOuts = 2, kH = 0;
 };
 template <> struct Cfg<kBwd> {
-  static constexpr int kStages = 3, kEpiWarps = 16, kOuts = 1, kH = 1;
+  static constexpr int kStages1 = 3, kStages2 = 4, kEpiWarps = 16, kOuts = 1, kH = 1;
 };
 
+template <int kMode, int kPair>
+__host__ __device__ constexpr int stages_of() {
+  return kPair == 2 ? Cfg<kMode>::kStages2 : Cfg<kMode>::kStages1;
+}
+// With two CTAs per tile each CTA holds half of B's 256 rows (the MMA reads both halves).
+template <int kPair>
+__host__ __device__ constexpr uint32_t b_bytes() {
+  return uint32_t(kBN / kPair) * kBK * 2;
+}
+
 template <int kMode>
-constexpr int threads_of() {
+__host__ __device__ constexpr int threads_of() {
   return (kEpiWarp0 + Cfg<kMode>::kEpiWarps) * 32;
 }
 
-template <int kMode>
-constexpr uint32_t smem_bytes() {
-  return 1024 + Cfg<kMode>::kStages * (kABytes + kBBytes) +
+template <int kMode, int kPair>
+__host__ __device__ constexpr uint32_t smem_bytes() {
+  return 1024 + stages_of<kMode, kPair>() * (kABytes + b_bytes<kPair>()) +
          Cfg<kMode>::kEpiWarps * (Cfg<kMode>::kOuts + Cfg<kMode>::kH) * kTileBytes + kBarBytes;
 }
-static_assert(smem_bytes<kPlain>() <= 227 * 1024, "plain shared memory");
-static_assert(smem_bytes<kFwd>() <= 227 * 1024, "forward shared memory");
-static_assert(smem_bytes<kBwd>() <= 227 * 1024, "backward shared memory");
+static_assert(smem_bytes<kPlain, 1>() <= 227 * 1024, "plain shared memory");
+static_assert(smem_bytes<kFwd, 1>() <= 227 * 1024, "forward shared memory");
+static_assert(smem_bytes<kBwd, 1>() <= 227 * 1024, "backward shared memory");
+static_assert(smem_bytes<kPlain, 2>() <= 227 * 1024, "plain shared memory (pairs)");
+static_assert(smem_bytes<kFwd, 2>() <= 227 * 1024, "forward shared memory (pairs)");
+static_assert(smem_bytes<kBwd, 2>() <= 227 * 1024, "backward shared memory (pairs)");
 
 struct GemmArgs {
   int32_t m;            // rows of A and of the outputs
-  int32_t m_tiles;      // row tiles (ceil(M / 128))
+  int32_t m_tiles;      // row tiles (ceil(M / (128 x CTAs per tile)))
   int32_t n_tiles;      // column tiles (N / 256)
   int32_t num_tiles;    // row tiles x column tiles
   int32_t k_blocks;     // K / 64
@@ -211,32 +224,89 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// Tensor memory, MMA and commit for one CTA (kPair = 1) or a CTA pair of a cluster (kPair = 2:
+// issued by the pair's rank-0 CTA, operands and accumulator split across both CTAs).
+template <int kPair>
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                   smem_u32(slot)),
-               "r"(cols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  if constexpr (kPair == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)), "r"(cols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(slot)), "r"(cols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
 }
+template <int kPair>
 __device__ __forceinline__ void tmem_free(uint32_t base, uint32_t cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
-               : "memory");
+  if constexpr (kPair == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
+                 : "memory");
+  }
 }
 // D[tmem] (+)= A[smem] B[smem]^T for one K = 16 slice.
+template <int kPair>
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (kPair == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
-// Arrive once on `bar` when every MMA this thread issued so far has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+// Arrive once on the mbarrier at shared::cluster address `bar` (this CTA's or the pair peer's)
+// when every MMA this thread issued so far has completed.
+template <int kPair>
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  if constexpr (kPair == 1) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar) : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar) : "memory");
+  }
+}
+// shared::cluster address of the object at `p` in the cluster's CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the pair's rank-0
+// barrier `bar` (a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t x, int32_t y) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
 // 16 consecutive fp32 columns of this thread's TMEM lane; the values are valid after
@@ -271,9 +341,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 // Instruction descriptor: fp32 accumulator (bits 4-5 = 1), A and B bf16 (7-9 = 1, 10-12 = 1),
-// both K-major (15, 16 = 0), N >> 3 in 17-22, M >> 4 in 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
-                            (uint32_t(kBM >> 4) << 24);
+// both K-major (15, 16 = 0), N >> 3 in 17-22, M >> 4 in 24-28 (M = 256 for a CTA pair).
+template <int kPair>
+__host__ __device__ constexpr uint32_t idesc_of() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
+         (uint32_t((kBM * kPair) >> 4) << 24);
+}
 
 // Byte offset of 16-byte granule j (0..3) of row r in a 64-byte-swizzled tile (the TMA
 // SWIZZLE_64B pattern: granule index XOR address bits 7-8).
@@ -289,13 +362,14 @@ __device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) {
 // The kernel.
 // ---------------------------------------------------------------------------
 
-template <int kMode, int kF>
+template <int kMode, int kF, int kPair>
 __global__ void __launch_bounds__(threads_of<kMode>(), 1)
 kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_out0,
                 const __grid_constant__ CUtensorMap tm_out1,
                 const __grid_constant__ CUtensorMap tm_h, const GemmArgs args) {
-  constexpr int S = Cfg<kMode>::kStages;
+  constexpr int S = stages_of<kMode, kPair>();
+  constexpr uint32_t kBBytes = b_bytes<kPair>();
   constexpr int kOuts = Cfg<kMode>::kOuts;
   constexpr int kEpiWarps = Cfg<kMode>::kEpiWarps;
   constexpr int kSlice = kBN / (kEpiWarps / 4);  // columns per epilogue warp and tile
@@ -308,10 +382,10 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   uint8_t* s_out = s_b + S * kBBytes;                  // [epilogue warp][kOuts] 32 x 32 tiles
   uint8_t* s_h = s_out + kEpiWarps * kOuts * kTileBytes;  // backward: [epilogue warp] h tile
   uint64_t* bars = reinterpret_cast<uint64_t*>(s_h + kEpiWarps * Cfg<kMode>::kH * kTileBytes);
-  uint64_t* full = bars;              // [S]  TMA -> MMA
-  uint64_t* empty = full + S;         // [S]  MMA -> TMA
-  uint64_t* tfull = empty + S;        // [2]  MMA -> epilogue
-  uint64_t* tempty = tfull + 2;       // [2]  epilogue warps -> MMA
+  uint64_t* full = bars;              // [S]  TMA -> MMA (rank 0's counts both CTAs' bytes)
+  uint64_t* empty = full + S;         // [S]  MMA -> TMA (in each CTA)
+  uint64_t* tfull = empty + S;        // [2]  MMA -> epilogue (in each CTA)
+  uint64_t* tempty = tfull + 2;       // [2]  epilogue warps of both CTAs -> MMA (rank 0's)
   uint64_t* hbar = tempty + 2;        // [kEpiWarps] backward h loads
   uint64_t* drain = hbar + kEpiWarps; // MMA completion before teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -319,6 +393,9 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair == 2 ? cluster_rank() : 0u;   // position in the CTA pair
+  const int slot0 = int(blockIdx.x) / kPair;                 // tile slot of this CTA (pair)
+  const int slots = int(gridDim.x) / kPair;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -327,7 +404,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     }
     for (int j = 0; j < 2; ++j) {
       mbar_init(tfull + j, 1);
-      mbar_init(tempty + j, kEpiWarps);
+      mbar_init(tempty + j, kPair * kEpiWarps);
     }
     for (int j = 0; j < kEpiWarps; ++j) mbar_init(hbar + j, 1);
     mbar_init(drain, 1);
@@ -339,9 +416,10 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     if (kMode == kFwd) prefetch_map(&tm_out1);
     if (kMode == kBwd) prefetch_map(&tm_h);
   }
-  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == 1) tmem_alloc<kPair>(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair == 2) cluster_sync();  // the peer's barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -350,32 +428,44 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   const int k_blocks = args.k_blocks;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (each CTA loads its A rows and its half of B) ----------------
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile % m_tiles) * kBM;
-        const int n0 = (tile / m_tiles) * kBN;
+      for (int tile = slot0; tile < num_tiles; tile += slots) {
+        const int m0 = (tile % m_tiles) * (kBM * kPair) + int(rank) * kBM;
+        const int n0 = (tile / m_tiles) * kBN + int(rank) * (kBN / kPair);
         bool ok = true;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!wait_phase(empty + stage, phase ^ 1u, abort)) { ok = false; break; }
-          mbar_expect_tx(full + stage, kABytes + kBBytes);
-          tma_load_2d(s_a + stage * kABytes, &tm_a, full + stage, kb * kBK, m0);
-          tma_load_2d(s_b + stage * kBBytes, &tm_b, full + stage, kb * kBK, n0);
+          if constexpr (kPair == 1) {
+            mbar_expect_tx(full + stage, kABytes + kBBytes);
+            tma_load_2d(s_a + stage * kABytes, &tm_a, full + stage, kb * kBK, m0);
+            tma_load_2d(s_b + stage * kBBytes, &tm_b, full + stage, kb * kBK, n0);
+          } else {
+            if (rank == 0) mbar_expect_tx(full + stage, 2 * (kABytes + kBBytes));
+            const uint32_t bar0 = cluster_addr(full + stage, 0);
+            tma_load_2d_pair(s_a + stage * kABytes, &tm_a, bar0, kb * kBK, m0);
+            tma_load_2d_pair(s_b + stage * kBBytes, &tm_b, bar0, kb * kBK, n0);
+          }
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (rank 0 of a pair issues for both CTAs) ----------------
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool issued = false;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      // arrive on the barrier in this CTA and, for a pair, on the same barrier in the peer
+      auto commit_both = [&](uint64_t* bar) {
+        umma_commit<kPair>(cluster_addr(bar, 0));
+        if constexpr (kPair == 2) umma_commit<kPair>(cluster_addr(bar, 1));
+      };
+      for (int tile = slot0; tile < num_tiles; tile += slots, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!wait_phase(tempty + acc, acc_phase ^ 1u, abort)) break;
@@ -390,20 +480,20 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             // advance the start address by k x 32 bytes inside the swizzled 128-byte rows
-            umma_bf16(d_tmem, a_desc + uint64_t(k * 2), b_desc + uint64_t(k * 2), kIdesc,
-                      (kb | k) != 0 ? 1u : 0u);
+            umma_bf16<kPair>(d_tmem, a_desc + uint64_t(k * 2), b_desc + uint64_t(k * 2),
+                             idesc_of<kPair>(), (kb | k) != 0 ? 1u : 0u);
           }
           issued = true;
-          umma_commit(empty + stage);
+          commit_both(empty + stage);
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit(tfull + acc);
+        commit_both(tfull + acc);
       }
       if (issued) {
-        // Every MMA has completed before warp 1 frees the tensor memory (bounded by the clock
+        // Every MMA has completed before the tensor memory is freed (bounded by the clock
         // alone: on the normal path this returns at once).
-        umma_commit(drain);
+        umma_commit<kPair>(cluster_addr(drain, 0));
         const long long t0 = clock64();
         while (!mbar_try(drain, 0)) {
           if (clock64() - t0 > kWaitCycles) {
@@ -420,7 +510,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     const int slice = ew >> 2;                    // 64-column slice of the tile
     const int row = lane;                         // row within the warp's 32-row tile
     const uint32_t lane_addr = tmem_base + (uint32_t(quad * 32) << 16);
-    const int my_tiles = (num_tiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1;
+    const int my_tiles = slot0 < num_tiles ? (num_tiles - 1 - slot0) / slots + 1 : 0;
     const int total_chunks = my_tiles * kChunksPerSlice;
     uint8_t* stage_out = s_out + ew * kOuts * kTileBytes;
     uint8_t* stage_h = s_h + ew * kTileBytes;
@@ -432,11 +522,11 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
       for (int i = lane; i < args.groups * kAcc; i += 32) wpart[i] = 0.0;
       __syncwarp();
     }
-    // Chunk q of this warp: tile blockIdx.x + (q / chunks per slice) * grid, columns
+    // Chunk q of this warp: tile slot0 + (q / chunks per slice) * slots, columns
     // slice * kSlice + (q % chunks per slice) * 32, rows quad * 32 .. + 31 of that tile.
     auto chunk_origin = [&](int q, int& m0, int& n0) {
-      const int tile = blockIdx.x + (q / kChunksPerSlice) * gridDim.x;
-      m0 = (tile % m_tiles) * kBM + quad * kWarpRows;
+      const int tile = slot0 + (q / kChunksPerSlice) * slots;
+      m0 = (tile % m_tiles) * (kBM * kPair) + int(rank) * kBM + quad * kWarpRows;
       n0 = (tile / m_tiles) * kBN + slice * kSlice + (q % kChunksPerSlice) * kChunk;
     };
     auto issue_h = [&](int q) {
@@ -485,7 +575,8 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     int q = 0;
     int local = 0;
     bool alive = true;
-    for (int tile = blockIdx.x; tile < num_tiles && alive; tile += gridDim.x, ++local) {
+    const uint32_t tempty0 = cluster_addr(tempty, 0);  // rank 0's tempty[0]
+    for (int tile = slot0; tile < num_tiles && alive; tile += slots, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!warp_wait(tfull + acc, acc_phase)) break;
@@ -587,7 +678,10 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
           // this warp has read its part of the accumulator: hand it back to the MMA issuer
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(tempty + acc);
+          if (lane == 0) {
+            if constexpr (kPair == 1) mbar_arrive(tempty + acc);
+            else mbar_arrive_cluster(tempty0 + uint32_t(acc) * 8u);
+          }
         }
         do_half(vb, 1);
         fence_async_shared();
@@ -607,10 +701,11 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair == 2) cluster_sync();  // the pair is done with TMEM and remote barriers
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_free(tmem_base, kTmemCols);
+    tmem_free<kPair>(tmem_base, kTmemCols);
   }
   if constexpr (kMode == kBwd) {
     // This CTA's warp rows, added in warp order into its row 0 (the reduction kernel then
@@ -737,24 +832,125 @@ int check_groups(int64_t n, int32_t groups) {
   return KAT_OK;
 }
 
-int grid_for(int64_t m, int64_t n, int device) {
-  const int64_t tiles = ((m + kBM - 1) / kBM) * (n / kBN);
-  const int sms = sm_count(device);
-  if (sms <= 0) return 0;
-  return int(tiles < sms ? tiles : sms);
+// KAT_GEMM_CTA_PAIR=0 keeps one CTA per 128-row tile; by default a cluster's CTA pair shares
+// each 256-row tile (cta_group::2) whenever the device can co-schedule CTA pairs.
+bool pairs_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("KAT_GEMM_CTA_PAIR");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
 }
 
-template <int kMode, int kF>
-int launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& o0,
-           const CUtensorMap& o1, const CUtensorMap& h, const GemmArgs& args, int grid,
-           cudaStream_t stream) {
-  auto kernel = kat_gemm_kernel<kMode, kF>;
-  constexpr uint32_t smem = smem_bytes<kMode>();
+template <int kMode, int kF, int kPair>
+int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int64_t k,
+                const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& h,
+                GemmArgs args, int device, cudaStream_t stream, int* grid_out) {
+  auto kernel = kat_gemm_kernel<kMode, kF, kPair>;
+  constexpr uint32_t smem = smem_bytes<kMode, kPair>();
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
       cudaSuccess)
     return KAT_ERR_CUDA;
-  kernel<<<grid, threads_of<kMode>(), smem, stream>>>(a, b, o0, o1, h, args);
+  CUtensorMap mb;
+  if (!make_map(&mb, b, n, k, kBK, uint32_t(kBN / kPair), CU_TENSOR_MAP_SWIZZLE_128B))
+    return KAT_ERR_CUDA;
+  args.m_tiles = int32_t((m + kBM * kPair - 1) / (kBM * kPair));
+  args.num_tiles = int32_t(int64_t(args.m_tiles) * (n / kBN));
+  const int sms = sm_count(device);
+  if (sms <= 0) return KAT_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(threads_of<kMode>());
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  int slots = sms;
+  if constexpr (kPair == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static std::mutex mu;
+    static int cache[64] = {0};
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64) return KAT_ERR_CUDA;
+    if (cache[device] == 0) {
+      cfg.gridDim = dim3(2 * (sms / 2));
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+        clusters = -1;
+      cache[device] = clusters;
+    }
+    if (cache[device] < 0) return KAT_ERR_CUDA;
+    slots = cache[device];
+  }
+  if (slots > args.num_tiles) slots = args.num_tiles;
+  cfg.gridDim = dim3(uint32_t(slots * kPair));
+  if (cudaLaunchKernelEx(&cfg, kernel, ma, mb, o0, o1, h, args) != cudaSuccess)
+    return KAT_ERR_CUDA;
+  *grid_out = slots * kPair;
   return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+// Resident CTA pairs for this kernel on `device` (cluster occupancy, cached), or -1.
+template <int kMode, int kF>
+int pair_slots(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return -1;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    auto kernel = kat_gemm_kernel<kMode, kF, 2>;
+    constexpr uint32_t smem = smem_bytes<kMode, 2>();
+    int clusters = -1;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) ==
+        cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cfg.blockDim = dim3(threads_of<kMode>());
+      cfg.dynamicSmemBytes = smem;
+      cfg.gridDim = dim3(2 * uint32_t(sm_count(device) / 2));
+      int c = 0;
+      if (cudaOccupancyMaxActiveClusters(&c, kernel, &cfg) == cudaSuccess && c > 0) clusters = c;
+    }
+    cudaGetLastError();
+    cache[device] = clusters;
+  }
+  return cache[device];
+}
+
+// One CTA pair per 256-row tile when that takes no more waves of tiles than one CTA per
+// 128-row tile (pairs halve each CTA's B traffic, but a ragged last wave costs a whole tile
+// time), else one CTA per tile.  Every mode decides the same way for the same M, N, so the
+// plain GEMM and the fused kernels share their accumulation order.
+template <int kMode, int kF>
+int launch(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int64_t k,
+           const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& h,
+           const GemmArgs& args, int device, cudaStream_t stream, int* grid_out) {
+  if (pairs_enabled()) {
+    const int pairs = pair_slots<kPlain, kFormulaKat>(device);
+    const int sms = sm_count(device);
+    if (pairs > 0 && sms > 0) {
+      const int64_t t1 = ((m + kBM - 1) / kBM) * (n / kBN);
+      const int64_t t2 = ((m + 2 * kBM - 1) / (2 * kBM)) * (n / kBN);
+      const int64_t waves1 = (t1 + sms - 1) / sms;
+      const int64_t waves2 = (t2 + pairs - 1) / pairs;
+      if (waves2 <= waves1) {
+        const int rc = launch_mode<kMode, kF, 2>(ma, b, m, n, k, o0, o1, h, args, device,
+                                                stream, grid_out);
+        if (rc == KAT_OK) return rc;
+        cudaGetLastError();  // clear a refused cluster launch before the single-CTA launch
+      }
+    }
+  }
+  return launch_mode<kMode, kF, 1>(ma, b, m, n, k, o0, o1, h, args, device, stream, grid_out);
 }
 
 int current_device(int* dev) { return cudaGetDevice(dev) == cudaSuccess ? KAT_OK : KAT_ERR_CUDA; }
@@ -775,24 +971,20 @@ int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c, int64
     return KAT_ERR_BAD_SHAPE;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
-  const int grid = grid_for(m, n, dev);
-  if (grid <= 0) return KAT_ERR_CUDA;
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mc;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mc, c, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
   args.m = int32_t(m);
-  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
-  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
   args.group_width = int32_t(n);
   args.groups = 1;
   args.bias = static_cast<const uint16_t*>(bias);
-  return launch<kPlain, kFormulaKat>(ma, mb, mc, mc, mc, args, grid,
-                                     static_cast<cudaStream_t>(stream));
+  int grid = 0;
+  return launch<kPlain, kFormulaKat>(ma, b, m, n, k, mc, mc, mc, args, dev,
+                                     static_cast<cudaStream_t>(stream), &grid);
 }
 
 int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const float* num,
@@ -809,19 +1001,14 @@ int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const 
     return KAT_ERR_BAD_SHAPE;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
-  const int grid = grid_for(m, n, dev);
-  if (grid <= 0) return KAT_ERR_CUDA;
-  CUtensorMap ma, mb, mh, my;
+  CUtensorMap ma, mh, my;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mh, h, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&my, y, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
   args.m = int32_t(m);
-  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
-  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
   args.group_width = int32_t(n / num_groups);
   args.groups = num_groups;
@@ -829,17 +1016,18 @@ int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const 
   args.num = num;
   args.den = den;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int grid = 0;
   return formula == KAT_FORMULA_KAT
-             ? launch<kFwd, kFormulaKat>(ma, mb, mh, my, mh, args, grid, st)
-             : launch<kFwd, kFormulaAbsSum>(ma, mb, mh, my, mh, args, grid, st);
+             ? launch<kFwd, kFormulaKat>(ma, b, m, n, k, mh, my, mh, args, dev, st, &grid)
+             : launch<kFwd, kFormulaAbsSum>(ma, b, m, n, k, mh, my, mh, args, dev, st, &grid);
 }
 
 size_t kat_gemm_rational_bwd_workspace_bytes(int64_t m, int64_t n, int32_t num_groups,
                                              int device) {
   if (check_shape(m, n, kBK) != KAT_OK || num_groups < 1) return 0;
-  const int grid = grid_for(m, n, device);
-  if (grid <= 0) return 0;
-  return size_t(grid) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
+  const int sms = sm_count(device);  // the grid never exceeds one CTA per SM
+  if (sms <= 0) return 0;
+  return size_t(sms) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
 }
 
 int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const float* num,
@@ -855,22 +1043,19 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   if (!aligned16(a) || !aligned16(b) || !aligned16(h) || !aligned16(dh)) return KAT_ERR_BAD_SHAPE;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
-  const int grid = grid_for(m, n, dev);
-  if (grid <= 0) return KAT_ERR_CUDA;
-  const size_t need = size_t(grid) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
+  const int sms = sm_count(dev);
+  if (sms <= 0) return KAT_ERR_CUDA;
+  const size_t need = size_t(sms) * kMaxEpiWarps * size_t(num_groups) * kAcc * sizeof(double);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return KAT_ERR_WORKSPACE;
-  CUtensorMap ma, mb, mh, md;
+  CUtensorMap ma, mh, md;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mb, b, n, k, kBK, kBN, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_map(&mh, h, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&md, dh, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
   args.m = int32_t(m);
-  args.m_tiles = int32_t((m + kBM - 1) / kBM);
   args.n_tiles = int32_t(n / kBN);
-  args.num_tiles = int32_t(((m + kBM - 1) / kBM) * (n / kBN));
   args.k_blocks = int32_t(k / kBK);
   args.group_width = int32_t(n / num_groups);
   args.groups = num_groups;
@@ -878,9 +1063,11 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   args.den = den;
   args.partial = static_cast<double*>(workspace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int grid = 0;
   const int rc = formula == KAT_FORMULA_KAT
-                     ? launch<kBwd, kFormulaKat>(ma, mb, md, md, mh, args, grid, st)
-                     : launch<kBwd, kFormulaAbsSum>(ma, mb, md, md, mh, args, grid, st);
+                     ? launch<kBwd, kFormulaKat>(ma, b, m, n, k, md, md, mh, args, dev, st, &grid)
+                     : launch<kBwd, kFormulaAbsSum>(ma, b, m, n, k, md, md, mh, args, dev, st,
+                                                    &grid);
   if (rc != KAT_OK) return rc;
   const int rgrid = (num_groups + kReduceWarps - 1) / kReduceWarps;
   kat_gemm_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, st>>>(

@@ -261,7 +261,7 @@ def test_fused_abs_after_sum_formula(m, n, k, groups):
     bit-identical to the activation kernels' abs-after-sum path on the same h and g; the
     coefficient gradients within 1e-4 of the float64 restatement of that formula."""
     from oracle import rat_torch_oracle as rat
-    from rational_kat_cu_b200 import rat_cuda as rc
+    from rational_kat_cu_b200.rat_cuda import rat_bwd_cuda, rat_fwd_cuda
 
     gen = torch.Generator(device="cuda").manual_seed(m + 7 * n)
     a = _bf16((m, k), gen)
@@ -271,11 +271,11 @@ def test_fused_abs_after_sum_formula(m, n, k, groups):
     f = _native.KAT_FORMULA_ABS_SUM
     h, y = fg.gemm_rational_fwd(a, b, None, num, den, groups, formula=f)
     assert torch.equal(h, fg.gemm_bf16(a, b))
-    assert torch.equal(y, rc.rat_fwd_cuda(h, num, den, groups))
+    assert torch.equal(y, rat_fwd_cuda(h, num, den, groups))
     gout = _bf16((m, k), gen, 0.1)
     dh, d_num, d_den = fg.gemm_rational_bwd(gout, b, h, num, den, groups, formula=f)
     g = fg.gemm_bf16(gout, b)
-    dx_ref, dn_ref, dd_ref = rc.rat_bwd_cuda(h, num, den, g, groups)
+    dx_ref, dn_ref, dd_ref = rat_bwd_cuda(h, num, den, g, groups)
     torch.cuda.synchronize()
     assert torch.equal(dh, dx_ref)
     _, _, da64, db64 = rat.rat_forward_backward(h.float().cpu(), num[0].cpu(), den.cpu(),
@@ -285,3 +285,53 @@ def test_fused_abs_after_sum_formula(m, n, k, groups):
                                           g.float().cpu())
     assert_coef_grads(d_num.cpu(), da64, nmag, "abs-sum d_num")
     assert_coef_grads(d_den.cpu(), db64, dmag, "abs-sum d_den")
+
+
+PAIR_CHILD = r'''
+import sys
+sys.path.insert(0, {repo!r})
+import torch
+import rational_kat_cu_b200 as kat
+from rational_kat_cu_b200 import fused_gemm as fg
+g = torch.Generator(device="cuda").manual_seed(21)
+m, n, k, G = 1000, 768, 256, 8
+a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+b = (torch.randn(n, k, generator=g, device="cuda") * k ** -0.5).to(torch.bfloat16)
+go = (torch.randn(m, k, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+act = kat.KAT_Group(num_groups=G, mode="gelu").cuda()
+num = act.weight_numerator.detach().repeat(G, 1).contiguous()
+den = act.weight_denominator.detach().contiguous()
+h, y = fg.gemm_rational_fwd(a, b, None, num, den, G)
+dh, dn, dd = fg.gemm_rational_bwd(go, b, h, num, den, G)
+torch.cuda.synchronize()
+assert fg.device_status(0) == 0
+torch.save({{"h": h.cpu(), "y": y.cpu(), "dh": dh.cpu(), "dn": dn.cpu(), "dd": dd.cpu()}}, {out!r})
+'''
+
+
+def test_cta_pair_and_single_cta_tiles_agree(tmp_path):
+    """The same problem with CTA-pair tiles (cta_group::2, the default where they take no more
+    waves) and with one CTA per tile (KAT_GEMM_CTA_PAIR=0): both within the GEMM bound of a
+    float64 product, and the fused outputs consistent with each one's own h."""
+    import os
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = {}
+    for pair in ("1", "0"):
+        out = str(tmp_path / f"pair{pair}.pt")
+        env = dict(os.environ, KAT_GEMM_CTA_PAIR=pair)
+        res = subprocess.run([sys.executable, "-c", PAIR_CHILD.format(repo=repo, out=out)],
+                             env=env, capture_output=True, text=True, timeout=600)
+        assert res.returncode == 0, res.stdout + res.stderr
+        outs[pair] = torch.load(out)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    m, n, k = 1000, 768, 256
+    a = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    b = (torch.randn(n, k, generator=g, device="cuda") * k ** -0.5).to(torch.bfloat16)
+    ref, tol = _gemm_bound(a.cpu(), b.cpu(), None)
+    for pair, o in outs.items():
+        assert bool(((o["h"].double() - ref).abs() <= tol).all()), pair
+    d = (outs["1"]["dn"].double() - outs["0"]["dn"].double()).abs()
+    assert float((d / outs["0"]["dn"].double().abs().clamp_min(1e-3)).max()) < 1e-3
