@@ -606,27 +606,34 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             load_fwd_coef<float2, kF>(args.num, args.den, g, fc);
           }
         }
+        // The chunk's 32 bias values (zeros without a bias), loaded before the accumulator so
+        // their latency overlaps the TMEM loads.
+        uint4 bias_words[4];
+        if constexpr (kMode == kPlain || kMode == kFwd) {
+          if (args.bias != nullptr) {
+            const uint4* bp = reinterpret_cast<const uint4*>(args.bias + n0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bias_words[j] = __ldg(bp + j);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bias_words[j] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
         // One 16-column half: epilogue math on v, bf16 words into the staging tile(s).
         auto do_half = [&](uint32_t (&v)[16], const int half) {
           uint32_t w0[8];
           uint32_t w1[8];
           if constexpr (kMode == kPlain || kMode == kFwd) {
             float bias[16];
-            if (args.bias != nullptr) {
-              const uint4* bp = reinterpret_cast<const uint4*>(args.bias + n0 + half * kHalf);
 #pragma unroll
-              for (int j = 0; j < 2; ++j) {
-                const uint4 u = __ldg(bp + j);
-                const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+            for (int j = 0; j < 2; ++j) {
+              const uint4 u = bias_words[half * 2 + j];
+              const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  bias[j * 8 + t * 2] = bf16_bits_to_float(uw[t] & 0xFFFFu);
-                  bias[j * 8 + t * 2 + 1] = bf16_bits_to_float(uw[t] >> 16);
-                }
+              for (int t = 0; t < 4; ++t) {
+                bias[j * 8 + t * 2] = bf16_bits_to_float(uw[t] & 0xFFFFu);
+                bias[j * 8 + t * 2 + 1] = bf16_bits_to_float(uw[t] >> 16);
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) bias[j] = 0.0f;
             }
 #pragma unroll
             for (int p = 0; p < 8; ++p) {
