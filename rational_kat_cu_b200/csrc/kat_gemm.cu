@@ -17,9 +17,9 @@
 //                      epilogue warps per SM sub-partition keep the FP32 pipe busy while the
 //                      tensor pipe runs the next tile.
 // With two accumulators the epilogue of one output tile overlaps the mainloop of the next.
-// Tiles are numbered column-block-major (consecutive tiles share a 256-column block of B, so a
-// CTA's tiles c, c + grid, c + 2 grid, ... mostly stay in one block of channel groups); A and
-// B are re-read from L2.
+// Tiles are numbered column-block-major and every CTA (pair) takes one contiguous run of them,
+// so a CTA's tiles mostly share one 256-column block of B and one set of channel groups (few
+// coefficient reloads and gradient flushes); A and B are re-read from L2.
 //
 // Epilogues: plain (C = bf16(acc + bias)); forward (h = bf16(acc + bias), y = rational(h) with
 // the activation kernels' per-element math, so y is bit-identical to kat_rational_fwd on h);
@@ -396,6 +396,10 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   const uint32_t rank = kPair == 2 ? cluster_rank() : 0u;   // position in the CTA pair
   const int slot0 = int(blockIdx.x) / kPair;                 // tile slot of this CTA (pair)
   const int slots = int(gridDim.x) / kPair;
+  // Each slot takes one contiguous run of the column-block-major tile order (an even split),
+  // so its tiles mostly share one 256-column block and one set of channel groups.
+  const int tile_begin = int(int64_t(slot0) * args.num_tiles / slots);
+  const int tile_end = int(int64_t(slot0 + 1) * args.num_tiles / slots);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -424,7 +428,6 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = args.m_tiles;
-  const int num_tiles = args.num_tiles;
   const int k_blocks = args.k_blocks;
 
   if (warp == 0) {
@@ -432,7 +435,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = slot0; tile < num_tiles; tile += slots) {
+      for (int tile = tile_begin; tile < tile_end; ++tile) {
         const int m0 = (tile % m_tiles) * (kBM * kPair) + int(rank) * kBM;
         const int n0 = (tile / m_tiles) * kBN + int(rank) * (kBN / kPair);
         bool ok = true;
@@ -465,7 +468,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
         umma_commit<kPair>(cluster_addr(bar, 0));
         if constexpr (kPair == 2) umma_commit<kPair>(cluster_addr(bar, 1));
       };
-      for (int tile = slot0; tile < num_tiles; tile += slots, ++local) {
+      for (int tile = tile_begin; tile < tile_end; ++tile, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!wait_phase(tempty + acc, acc_phase ^ 1u, abort)) break;
@@ -510,8 +513,6 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     const int slice = ew >> 2;                    // 64-column slice of the tile
     const int row = lane;                         // row within the warp's 32-row tile
     const uint32_t lane_addr = tmem_base + (uint32_t(quad * 32) << 16);
-    const int my_tiles = slot0 < num_tiles ? (num_tiles - 1 - slot0) / slots + 1 : 0;
-    const int total_chunks = my_tiles * kChunksPerSlice;
     uint8_t* stage_out = s_out + ew * kOuts * kTileBytes;
     uint8_t* stage_h = s_h + ew * kTileBytes;
     uint64_t* my_hbar = hbar + ew;
@@ -522,22 +523,25 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
       for (int i = lane; i < args.groups * kAcc; i += 32) wpart[i] = 0.0;
       __syncwarp();
     }
-    // Chunk q of this warp: tile slot0 + (q / chunks per slice) * slots, columns
-    // slice * kSlice + (q % chunks per slice) * 32, rows quad * 32 .. + 31 of that tile.
-    auto chunk_origin = [&](int q, int& m0, int& n0) {
-      const int tile = slot0 + (q / kChunksPerSlice) * slots;
-      m0 = (tile % m_tiles) * (kBM * kPair) + int(rank) * kBM + quad * kWarpRows;
-      n0 = (tile / m_tiles) * kBN + slice * kSlice + (q % kChunksPerSlice) * kChunk;
+    // A tile's origin for this warp: rows quad * 32 .. + 31 of this CTA's 128 rows, columns
+    // slice * kSlice .. + kSlice - 1 (chunk c starts kChunk * c further).  Computed once per tile.
+    auto tile_origin = [&](int tile, int& m0, int& n_base) {
+      const int tm = tile % m_tiles;
+      const int tn = tile / m_tiles;
+      m0 = tm * (kBM * kPair) + int(rank) * kBM + quad * kWarpRows;
+      n_base = tn * kBN + slice * kSlice;
     };
-    auto issue_h = [&](int q) {
+    auto issue_h = [&](int m0, int n0) {
       if constexpr (kMode == kBwd) {
-        int m0, n0;
-        chunk_origin(q, m0, n0);
         mbar_expect_tx(my_hbar, kTileBytes);
         tma_load_2d(stage_h, &tm_h, my_hbar, n0, m0);
       }
     };
-    if (kMode == kBwd && lane == 0 && total_chunks > 0) issue_h(0);
+    if (kMode == kBwd && lane == 0 && tile_begin < tile_end) {
+      int m0, nb;
+      tile_origin(tile_begin, m0, nb);
+      issue_h(m0, nb);
+    }
 
     FwdCoef<float2> fc;
     BwdCoef<float2> bc;
@@ -576,14 +580,15 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     int local = 0;
     bool alive = true;
     const uint32_t tempty0 = cluster_addr(tempty, 0);  // rank 0's tempty[0]
-    for (int tile = slot0; tile < num_tiles && alive; tile += slots, ++local) {
+    for (int tile = tile_begin; tile < tile_end && alive; ++tile, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      int m0, n_base;
+      tile_origin(tile, m0, n_base);
       if (!warp_wait(tfull + acc, acc_phase)) break;
       tc_fence_after();
       for (int c = 0; c < kChunksPerSlice; ++c, ++q) {
-        int m0, n0;
-        chunk_origin(q, m0, n0);
+        const int n0 = n_base + c * kChunk;
         const int g = n0 / args.group_width;
         uint32_t hw[16];
         if constexpr (kMode == kBwd) {
@@ -594,7 +599,15 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             hw[j * 4 + 0] = u.x; hw[j * 4 + 1] = u.y; hw[j * 4 + 2] = u.z; hw[j * 4 + 3] = u.w;
           }
           __syncwarp();  // the h tile is in registers: load the next chunk's into it
-          if (lane == 0 && q + 1 < total_chunks) issue_h(q + 1);
+          if (lane == 0) {
+            if (c + 1 < kChunksPerSlice) {
+              issue_h(m0, n0 + kChunk);
+            } else if (tile + 1 < tile_end) {
+              int nm0, nnb;
+              tile_origin(tile + 1, nm0, nnb);
+              issue_h(nm0, nnb);
+            }
+          }
           if (g != cur_group) {
             if (cur_group >= 0) flush(cur_group);
             cur_group = g;
