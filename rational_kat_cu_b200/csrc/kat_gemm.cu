@@ -122,6 +122,7 @@ struct GemmArgs {
   const float* num;       // [G, 6]
   const float* den;       // [G, 4]
   double* partial;        // backward: [grid][16 warps][G][10]; row 0 of a CTA ends as its sum
+  int32_t stall;          // test hook: the MMA issuer waits on a barrier nothing completes
 };
 
 __device__ int g_gemm_status;
@@ -458,7 +459,11 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (rank 0 of a pair issues for both CTAs) ----------------
-    if (lane == 0 && rank == 0) {
+    if (lane == 0 && rank == 0 && args.stall) {
+      // Test hook (KAT_GEMM_TEST_STALL=1): a wait that nothing completes runs out, sets the
+      // abort flag and the device status, and every role stops at its next wait.
+      (void)wait_phase(drain, 0u, abort);
+    } else if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -874,6 +879,8 @@ int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int6
   CUtensorMap mb;
   if (!make_map(&mb, b, n, k, kBK, uint32_t(kBN / kPair), CU_TENSOR_MAP_SWIZZLE_128B))
     return KAT_ERR_CUDA;
+  const char* stall = getenv("KAT_GEMM_TEST_STALL");
+  args.stall = (stall != nullptr && stall[0] == '1') ? 1 : 0;
   args.m_tiles = int32_t((m + kBM * kPair - 1) / (kBM * kPair));
   args.num_tiles = int32_t(int64_t(args.m_tiles) * (n / kBN));
   const int sms = sm_count(device);

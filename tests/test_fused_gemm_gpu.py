@@ -335,3 +335,48 @@ def test_cta_pair_and_single_cta_tiles_agree(tmp_path):
         assert bool(((o["h"].double() - ref).abs() <= tol).all()), pair
     d = (outs["1"]["dn"].double() - outs["0"]["dn"].double()).abs()
     assert float((d / outs["0"]["dn"].double().abs().clamp_min(1e-3)).max()) < 1e-3
+
+
+STALL_CHILD = r'''
+import os, sys, time
+sys.path.insert(0, {repo!r})
+import torch
+from rational_kat_cu_b200 import _native
+from rational_kat_cu_b200 import fused_gemm as fg
+a = torch.randn(300, 128, device="cuda").to(torch.bfloat16)
+b = (torch.randn(512, 128, device="cuda") * 0.1).to(torch.bfloat16)
+assert fg.device_status(0, reset=True) == 0
+os.environ["KAT_GEMM_TEST_STALL"] = "1"
+t0 = time.time()
+fg.gemm_bf16(a, b)
+torch.cuda.synchronize()
+waited = time.time() - t0
+status = fg.device_status(0, reset=True)
+del os.environ["KAT_GEMM_TEST_STALL"]
+c = fg.gemm_bf16(a, b)
+torch.cuda.synchronize()
+err = float((c.double() - a.double() @ b.double().t()).abs().max())
+print("result", status, round(waited, 2), err, fg.device_status(0))
+'''
+
+
+def test_stalled_pipeline_reports_and_recovers():
+    """A pipeline wait that nothing completes (test hook KAT_GEMM_TEST_STALL=1: the MMA issuer
+    waits on a barrier no one arrives at) runs out after its clock limit: the kernel returns,
+    the sticky status reads KAT_DEVICE_WAIT_TIMEOUT, tensor memory is freed, and the next
+    launch in the same context computes correctly."""
+    import os
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ)
+    env.pop("KAT_GEMM_TEST_STALL", None)
+    res = subprocess.run([sys.executable, "-c", STALL_CHILD.format(repo=repo)], env=env,
+                         capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0, res.stdout + res.stderr
+    line = [l for l in res.stdout.splitlines() if l.startswith("result")][-1].split()
+    status, waited, err, after = int(line[1]), float(line[2]), float(line[3]), int(line[4])
+    assert status == _native.KAT_DEVICE_WAIT_TIMEOUT
+    assert 0.5 < waited < 60.0
+    assert err < 0.05 and after == 0
