@@ -1,7 +1,7 @@
 // kat_gemm.cu — sm_100a tensor-core GEMM (C = A B^T, bf16 in, fp32 accumulate) with the
 // group-rational activation fused into its epilogue (C ABI: include/kat_gemm.h).
 //
-// One persistent CTA per SM, 576 threads in three roles:
+// One persistent CTA per SM (or one CTA pair per two SMs, below), three roles:
 //   warp 0, one lane   TMA producer: per k-block, a 128 x 64 tile of A and a 256 x 64 tile of B
 //                      (bf16, 128-byte swizzled rows) into a ring of shared-memory stages;
 //   warp 1, one lane   MMA issuer: tcgen05.mma (kind::f16, M = 128, N = 256, K = 16) from the
@@ -9,24 +9,30 @@
 //                      accumulators in tensor memory; tcgen05.commit frees the stage when its
 //                      MMAs have read it and, after the last k-block, hands the accumulator to
 //                      the epilogue.  Warp 1 also allocates and frees the 512 TMEM columns;
-//   warps 2-17         epilogue, 16 independent warps: warp w owns the 32 accumulator rows of
-//                      its TMEM lane quadrant (a warp may read only lanes 32 (w % 4) .. + 31)
-//                      and one 64-column slice of the tile, which it reads 16 columns at a time
-//                      with tcgen05.ld, runs through the epilogue, writes as bf16 into its own
-//                      64-byte-swizzled 32 x 32 staging tile and stores with TMA (lane 0).  Four
-//                      epilogue warps per SM sub-partition keep the FP32 pipe busy while the
-//                      tensor pipe runs the next tile.
+//   warps 2 ..         epilogue, independent warps (8 for the plain and forward epilogues, 16
+//                      for the FP32-heavy backward): warp w owns the 32 accumulator rows of its
+//                      TMEM lane quadrant (a warp may read only lanes 32 (w % 4) .. + 31) and
+//                      one column slice of the tile, which it reads 16 columns at a time with
+//                      tcgen05.ld (the next load in flight while the previous half is
+//                      computed), runs through the epilogue, writes as bf16 into its own
+//                      64-byte-swizzled 32 x 32 staging tile and stores with TMA (lane 0).
 // With two accumulators the epilogue of one output tile overlaps the mainloop of the next.
 // Tiles are numbered column-block-major and every CTA (pair) takes one contiguous run of them,
 // so a CTA's tiles mostly share one 256-column block of B and one set of channel groups (few
 // coefficient reloads and gradient flushes); A and B are re-read from L2.
 //
+// CTA pairs (cta_group::2, a 2-CTA cluster per 256 x 256 tile): each CTA loads its 128 rows
+// of A and its half of B's rows, both CTAs' TMA loads count on the rank-0 CTA's barrier, the
+// rank-0 CTA issues M = 256 MMAs and commits to the barriers of both CTAs, each CTA's epilogue
+// reads its own 128 accumulator rows.  Used when 256-row tiles take no more waves than 128-row
+// tiles.
+//
 // Epilogues: plain (C = bf16(acc + bias)); forward (h = bf16(acc + bias), y = rational(h) with
 // the activation kernels' per-element math, so y is bit-identical to kat_rational_fwd on h);
 // backward (g = bf16(acc), the warp's 32 x 32 tile of h loaded by TMA one chunk ahead, dh = the
 // activation kernels' per-element backward on (h, g), per-thread fp32 gradient sums flushed in
-// a fixed order into per-warp fp64 partials, then a second kernel adds the partials of all
-// warps in a fixed order).
+// a fixed order into per-warp fp64 partials, summed per CTA in warp order at the end, then a
+// second kernel adds the CTA sums in a fixed order).
 //
 // Every mbarrier wait is bounded (about two seconds of clock cycles).  A wait that runs out
 // sets the CTA's abort flag and the sticky device status word; the other roles see the flag
