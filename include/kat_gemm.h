@@ -51,7 +51,8 @@ int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c,
 /* fc1 + act2 forward: h = A B^T + bias (bias may be NULL), y = rational(h).  Replaces the
  * GEMM followed by kat_rational/kat_1dgroup_triton.py:80-87 (KAT_Group.forward) on its output;
  * h is kept for the backward as the reference's autograd keeps the activation input
- * (rational_triton.py:250-251). */
+ * (rational_triton.py:250-251).  h may be NULL when no backward follows (inference): only y is
+ * written. */
 int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias,
                           const float* num, const float* den, void* h, void* y,
                           int64_t m, int64_t n, int64_t k, int32_t num_groups,

@@ -129,6 +129,7 @@ struct GemmArgs {
   const float* den;       // [G, 4]
   double* partial;        // backward: [grid][16 warps][G][10]; row 0 of a CTA ends as its sum
   int32_t stall;          // test hook: the MMA issuer waits on a barrier nothing completes
+  int32_t store_h;        // forward: 0 = y only (inference), h is neither staged nor stored
 };
 
 __device__ int g_gemm_status;
@@ -685,10 +686,12 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
             if (lane == 0) bulk_wait_read<0>();
             __syncwarp();
           }
+          if (kMode != kFwd || args.store_h) {
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
-            *reinterpret_cast<uint4*>(stage_out + sw64_offset(row, half * 2 + j)) =
-                make_uint4(w0[j * 4], w0[j * 4 + 1], w0[j * 4 + 2], w0[j * 4 + 3]);
+            for (int j = 0; j < 2; ++j)
+              *reinterpret_cast<uint4*>(stage_out + sw64_offset(row, half * 2 + j)) =
+                  make_uint4(w0[j * 4], w0[j * 4 + 1], w0[j * 4 + 2], w0[j * 4 + 3]);
+          }
           if constexpr (kMode == kFwd) {
 #pragma unroll
             for (int j = 0; j < 2; ++j)
@@ -718,7 +721,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
         fence_async_shared();
         __syncwarp();
         if (lane == 0 && m0 < args.m) {  // rows past M: nothing to store (tail tile)
-          tma_store_2d(&tm_out0, stage_out, n0, m0);
+          if (kMode != kFwd || args.store_h) tma_store_2d(&tm_out0, stage_out, n0, m0);
           if constexpr (kMode == kFwd) tma_store_2d(&tm_out1, stage_out + kTileBytes, n0, m0);
           bulk_commit();
         }
@@ -1023,24 +1026,24 @@ int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c, int64
 int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const float* num,
                           const float* den, void* h, void* y, int64_t m, int64_t n, int64_t k,
                           int32_t num_groups, int32_t formula, void* stream) {
-  if (a == nullptr || b == nullptr || num == nullptr || den == nullptr || h == nullptr ||
-      y == nullptr)
+  if (a == nullptr || b == nullptr || num == nullptr || den == nullptr || y == nullptr)
     return KAT_ERR_NULL_POINTER;
   if (formula != KAT_FORMULA_KAT && formula != KAT_FORMULA_ABS_SUM) return KAT_ERR_BAD_FORMULA;
   if (int st = check_shape(m, n, k)) return st;
   if (int st = check_groups(n, num_groups)) return st;
-  if (!aligned16(a) || !aligned16(b) || !aligned16(h) || !aligned16(y) ||
+  if (!aligned16(a) || !aligned16(b) || (h != nullptr && !aligned16(h)) || !aligned16(y) ||
       (bias != nullptr && !aligned16(bias)))
     return KAT_ERR_BAD_SHAPE;
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   CUtensorMap ma, mh, my;
   if (!make_map(&ma, a, m, k, kBK, kBM, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mh, h, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&mh, h != nullptr ? h : y, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&my, y, m, n, kChunk, kWarpRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return KAT_ERR_CUDA;
   GemmArgs args{};
   args.m = int32_t(m);
+  args.store_h = h != nullptr ? 1 : 0;
   args.n_tiles = int32_t(n / kBN);
   args.k_blocks = int32_t(k / kBK);
   args.group_width = int32_t(n / num_groups);

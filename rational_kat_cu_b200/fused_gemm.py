@@ -98,22 +98,23 @@ def gemm_bf16(a: Tensor, b: Tensor, bias: Optional[Tensor] = None) -> Tensor:
 
 
 def gemm_rational_fwd(a: Tensor, b: Tensor, bias: Optional[Tensor], num: Tensor, den: Tensor,
-                      num_groups: int, formula: int = _native.KAT_FORMULA_KAT
-                      ) -> Tuple[Tensor, Tensor]:
-    """h = a b^T + bias and y = P(h)/Q(h) per column group; returns (h, y), both bf16 [M, N]."""
+                      num_groups: int, formula: int = _native.KAT_FORMULA_KAT,
+                      need_h: bool = True) -> Tuple[Optional[Tensor], Tensor]:
+    """h = a b^T + bias and y = P(h)/Q(h) per column group; returns (h, y), both bf16 [M, N].
+    With need_h=False (no backward follows) only y is written and h is None."""
     a = _mat(a.detach(), "a")
     b = _mat(b.detach(), "b")
     m, n, k = _shapes(a, b)
     nf, df = _coef(num, den, num_groups, n)
     if bias is not None:
         bias = bias.detach().to(torch.bfloat16).contiguous()
-    h = torch.empty(m, n, device=a.device, dtype=torch.bfloat16)
-    y = torch.empty_like(h)
+    y = torch.empty(m, n, device=a.device, dtype=torch.bfloat16)
+    h = torch.empty_like(y) if need_h else None
     with torch.cuda.device(a.device):
         st = _native.lib().kat_gemm_rational_fwd(
             a.data_ptr(), b.data_ptr(), bias.data_ptr() if bias is not None else None,
-            nf.data_ptr(), df.data_ptr(), h.data_ptr(), y.data_ptr(), m, n, k, num_groups,
-            formula, _stream(a.device))
+            nf.data_ptr(), df.data_ptr(), h.data_ptr() if h is not None else None,
+            y.data_ptr(), m, n, k, num_groups, formula, _stream(a.device))
     _native.check("kat_gemm_rational_fwd", st)
     return h, y
 
@@ -193,10 +194,18 @@ class KANMlpFused(torch.autograd.Function):
 
 
 def kan_mlp_fused(x: Tensor, fc1: torch.nn.Linear, act2, fc2: torch.nn.Linear) -> Tensor:
-    """fc2(act2(fc1(x))) for x [..., C] through `KANMlpFused` (act2 a `KAT_Group`)."""
+    """fc2(act2(fc1(x))) for x [..., C] through `KANMlpFused` (act2 a `KAT_Group`).  When no
+    gradient is needed (inference) the forward GEMM writes y only."""
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
     g = act2.num_groups
+    params = (x, fc1.weight, fc1.bias, act2.weight_numerator, act2.weight_denominator,
+              fc2.weight, fc2.bias)
+    if not (torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in params)):
+        _, y = gemm_rational_fwd(x2, fc1.weight, fc1.bias, act2.weight_numerator.repeat(g, 1),
+                                 act2.weight_denominator, g, need_h=False)
+        out = F.linear(y, fc2.weight, fc2.bias)
+        return out.reshape(*shape[:-1], out.shape[-1])
     out = KANMlpFused.apply(x2, fc1.weight, fc1.bias, act2.weight_numerator.repeat(g, 1),
                             act2.weight_denominator, fc2.weight, fc2.bias, g,
                             _native.KAT_FORMULA_KAT)

@@ -380,3 +380,19 @@ def test_stalled_pipeline_reports_and_recovers():
     assert status == _native.KAT_DEVICE_WAIT_TIMEOUT
     assert 0.5 < waited < 60.0
     assert err < 0.05 and after == 0
+
+
+def test_inference_forward_writes_y_only():
+    """h = NULL (no backward follows): y identical to the h-storing forward; the KAN block
+    under no_grad takes this form and matches the training-mode output."""
+    a, b, bias, num, den = _fwd_case(333, 3072, 768, 8, seed=77)
+    h, y = fg.gemm_rational_fwd(a, b, bias, num, den, 8)
+    none, y2 = fg.gemm_rational_fwd(a, b, bias, num, den, 8, need_h=False)
+    torch.cuda.synchronize()
+    assert none is None and torch.equal(y, y2)
+    fc1, act2, fc2 = _kan_block(768, 3072, 8, seed=3)
+    x = _bf16((2 * 197, 768), torch.Generator(device="cuda").manual_seed(4))
+    with torch.no_grad():
+        out_inf = fg.kan_mlp_fused(x, fc1, act2, fc2)
+    out_train = fg.kan_mlp_fused(x.clone().requires_grad_(True), fc1, act2, fc2)
+    assert torch.equal(out_inf, out_train.detach())
