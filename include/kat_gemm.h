@@ -26,7 +26,8 @@
  * operands) and dh is exactly what kat_rational_bwd gives for (h, g); the coefficient gradients
  * are fixed-order fp64 sums of fp32 per-thread partials, bit-reproducible on one GPU model.
  *
- * Shapes: M >= 1; N a multiple of 256; K a multiple of 64; N / num_groups a multiple of 32;
+ * Shapes: M >= 0 (M = 0 is a no-op; the backward then writes zero coefficient gradients); N a
+ * multiple of 256; K a multiple of 64; N / num_groups a multiple of 32;
  * M, N, K below 2^31.  Pointers (bias included) 16-byte aligned, else KAT_ERR_BAD_SHAPE (a TMA
  * tensor map needs it).  Same conventions as
  * kat_rational.h: the caller owns every buffer (the backward's workspace included), nothing is

@@ -852,7 +852,7 @@ int sm_count(int device) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_shape(int64_t m, int64_t n, int64_t k) {
-  if (m < 1 || n < kBN || k < kBK) return KAT_ERR_BAD_SHAPE;
+  if (m < 0 || n < kBN || k < kBK) return KAT_ERR_BAD_SHAPE;
   if (n % kBN != 0 || k % kBK != 0) return KAT_ERR_BAD_SHAPE;
   if (m >= (int64_t(1) << 31) || n >= (int64_t(1) << 31) || k >= (int64_t(1) << 31))
     return KAT_ERR_BAD_SHAPE;
@@ -1005,6 +1005,7 @@ int kat_gemm_bf16(const void* a, const void* b, const void* bias, void* c, int64
   if (int st = check_shape(m, n, k)) return st;
   if (!aligned16(a) || !aligned16(b) || !aligned16(c) || (bias != nullptr && !aligned16(bias)))
     return KAT_ERR_BAD_SHAPE;
+  if (m == 0) return KAT_OK;  // empty problem: nothing to do
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   CUtensorMap ma, mc;
@@ -1034,6 +1035,7 @@ int kat_gemm_rational_fwd(const void* a, const void* b, const void* bias, const 
   if (!aligned16(a) || !aligned16(b) || (h != nullptr && !aligned16(h)) || !aligned16(y) ||
       (bias != nullptr && !aligned16(bias)))
     return KAT_ERR_BAD_SHAPE;
+  if (m == 0) return KAT_OK;  // empty problem: nothing to do
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   CUtensorMap ma, mh, my;
@@ -1077,6 +1079,13 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   if (int st = check_shape(m, n, k)) return st;
   if (int st = check_groups(n, num_groups)) return st;
   if (!aligned16(a) || !aligned16(b) || !aligned16(h) || !aligned16(dh)) return KAT_ERR_BAD_SHAPE;
+  if (m == 0) {  // empty problem: the coefficient gradients are zero sums
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(d_num, 0, size_t(num_groups) * 6 * sizeof(float), st) != cudaSuccess ||
+        cudaMemsetAsync(d_den, 0, size_t(num_groups) * 4 * sizeof(float), st) != cudaSuccess)
+      return KAT_ERR_CUDA;
+    return KAT_OK;
+  }
   int dev = 0;
   if (int st = current_device(&dev)) return st;
   const int sms = sm_count(dev);

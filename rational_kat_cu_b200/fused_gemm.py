@@ -55,7 +55,7 @@ def _shapes(a: Tensor, b: Tensor) -> Tuple[int, int, int]:
     if k != k2:
         raise ValueError(f"fused_gemm: inner dimensions differ: a {tuple(a.shape)}, "
                          f"b {tuple(b.shape)}")
-    if n % TILE_N or k % TILE_K or m < 1:
+    if n % TILE_N or k % TILE_K or m < 0:
         raise ValueError(f"fused_gemm: need N % {TILE_N} == 0 and K % {TILE_K} == 0, got "
                          f"M={m}, N={n}, K={k}")
     return m, n, k
@@ -63,7 +63,7 @@ def _shapes(a: Tensor, b: Tensor) -> Tuple[int, int, int]:
 
 def supports(m: int, n: int, k: int, num_groups: int = 1) -> bool:
     """Whether the fused kernels take an [m, k] x [n, k]^T problem with num_groups groups."""
-    return (m >= 1 and n % TILE_N == 0 and k % TILE_K == 0 and num_groups >= 1
+    return (m >= 0 and n % TILE_N == 0 and k % TILE_K == 0 and num_groups >= 1
             and n % num_groups == 0 and (n // num_groups) % CHUNK == 0)
 
 
@@ -89,6 +89,8 @@ def gemm_bf16(a: Tensor, b: Tensor, bias: Optional[Tensor] = None) -> Tensor:
     if bias is not None:
         bias = bias.detach().to(torch.bfloat16).contiguous()
     c = torch.empty(m, n, device=a.device, dtype=torch.bfloat16)
+    if m == 0:
+        return c
     with torch.cuda.device(a.device):
         st = _native.lib().kat_gemm_bf16(a.data_ptr(), b.data_ptr(),
                                          bias.data_ptr() if bias is not None else None,
@@ -110,6 +112,8 @@ def gemm_rational_fwd(a: Tensor, b: Tensor, bias: Optional[Tensor], num: Tensor,
         bias = bias.detach().to(torch.bfloat16).contiguous()
     y = torch.empty(m, n, device=a.device, dtype=torch.bfloat16)
     h = torch.empty_like(y) if need_h else None
+    if m == 0:
+        return h, y
     with torch.cuda.device(a.device):
         st = _native.lib().kat_gemm_rational_fwd(
             a.data_ptr(), b.data_ptr(), bias.data_ptr() if bias is not None else None,
@@ -132,6 +136,9 @@ def gemm_rational_bwd(a: Tensor, b: Tensor, h: Tensor, num: Tensor, den: Tensor,
         raise ValueError(f"fused_gemm: h shape {tuple(h.shape)} != {(m, n)}")
     nf, df = _coef(num, den, num_groups, n)
     dev = a.device
+    if m == 0:  # sums over no elements
+        return (torch.empty(0, n, device=dev, dtype=torch.bfloat16),
+                torch.zeros(num_groups, 6, device=dev), torch.zeros(num_groups, 4, device=dev))
     lib = _native.lib()
     ws_bytes = lib.kat_gemm_rational_bwd_workspace_bytes(m, n, num_groups, dev.index or 0)
     if ws_bytes == 0:

@@ -76,7 +76,7 @@ def test_gemm_entry_points_validate_before_launch():
     lib = _native.lib()
     E = _native
     P = 16  # an aligned address value; every call below has a bad argument, so none is used
-    for m, n, k in ((0, 256, 64), (128, 255, 64), (128, 256, 63), (128, 0, 64),
+    for m, n, k in ((-1, 256, 64), (128, 255, 64), (128, 256, 63), (128, 0, 64),
                     (1 << 31, 256, 64), (128, 256, 0)):
         assert lib.kat_gemm_bf16(P, P, None, P, m, n, k, None) == E.KAT_ERR_BAD_SHAPE
         assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, m, n, k, 8, 0, None) == \
@@ -98,6 +98,9 @@ def test_gemm_entry_points_validate_before_launch():
     for f in (-1, 2):
         assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, 128, 256, 64, 8, f, None) == \
             E.KAT_ERR_BAD_FORMULA
+    # an empty problem is a successful no-op (nothing is enqueued for the forward)
+    assert lib.kat_gemm_bf16(P, P, None, P, 0, 256, 64, None) == E.KAT_OK
+    assert lib.kat_gemm_rational_fwd(P, P, None, P, P, P, P, 0, 256, 64, 8, 0, None) == E.KAT_OK
     # TMA needs 16-byte aligned operands
     assert lib.kat_gemm_bf16(P + 2, P, None, P, 128, 256, 64, None) == E.KAT_ERR_BAD_SHAPE
     assert lib.kat_gemm_bf16(P, P, P + 8, P, 128, 256, 64, None) == E.KAT_ERR_BAD_SHAPE

@@ -16,7 +16,8 @@ from rational_kat_cu_b200 import grkan_vit as gv
     (128, 3072, 768, 64, False),      # 48 columns per group: not a multiple of 32
     (128, 300, 64, 1, False),         # N not a multiple of 256
     (128, 256, 100, 1, False),        # K not a multiple of 64
-    (0, 256, 64, 1, False),
+    (0, 256, 64, 1, True),           # empty batch: a no-op
+    (-1, 256, 64, 1, False),
     (128, 512, 64, 3, False),         # groups do not divide N
 ])
 def test_supported_shapes(m, n, k, g, ok):

@@ -396,3 +396,18 @@ def test_inference_forward_writes_y_only():
         out_inf = fg.kan_mlp_fused(x, fc1, act2, fc2)
     out_train = fg.kan_mlp_fused(x.clone().requires_grad_(True), fc1, act2, fc2)
     assert torch.equal(out_inf, out_train.detach())
+
+
+def test_empty_batch():
+    """M = 0: the forward returns empty outputs, the backward empty dh and zero coefficient
+    gradients (the sums over no elements), like the activation kernels' empty inputs."""
+    a = torch.empty(0, 128, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(512, 128, device="cuda").to(torch.bfloat16)
+    num, den = _coefs(8, torch.Generator(device="cuda").manual_seed(1))
+    h, y = fg.gemm_rational_fwd(a, b, None, num, den, 8)
+    assert h.shape == (0, 512) and y.shape == (0, 512)
+    dh, dn, dd = fg.gemm_rational_bwd(a, b, h, num, den, 8)
+    torch.cuda.synchronize()
+    assert dh.shape == (0, 512)
+    assert bool((dn == 0).all()) and bool((dd == 0).all())
+    assert fg.gemm_bf16(a, b).shape == (0, 512)
