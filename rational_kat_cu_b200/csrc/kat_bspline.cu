@@ -219,8 +219,9 @@ kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
   block_tiles(row_tiles * col_tiles, t0, t1);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int64_t loaded = -1;
+  // (column tile, row tile) of tile t0, then advanced one tile at a time (no division per tile)
+  int64_t ct = t0 / row_tiles, rt = t0 - (t0 / row_tiles) * row_tiles;
   for (int64_t tile = t0; tile < t1; ++tile) {
-    const int64_t ct = tile / row_tiles, rt = tile - ct * row_tiles;
     const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
     const int ncols = int(min(int64_t(kTileCols), features - c0));
     if (ct != loaded) {
@@ -256,6 +257,7 @@ kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
     __syncwarp();
     if (row < batch) warp_copy<true>(srow, out + row_offset(row, features, c0, nb), ncols * nb, lane);
     __syncwarp();
+    if (++rt == row_tiles) { rt = 0; ++ct; }
   }
 }
 
@@ -273,8 +275,9 @@ kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
   block_tiles(row_tiles * col_tiles, t0, t1);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int64_t loaded = -1;
+  // (column tile, row tile) of tile t0, then advanced one tile at a time (no division per tile)
+  int64_t ct = t0 / row_tiles, rt = t0 - (t0 / row_tiles) * row_tiles;
   for (int64_t tile = t0; tile < t1; ++tile) {
-    const int64_t ct = tile / row_tiles, rt = tile - ct * row_tiles;
     const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
     const int ncols = int(min(int64_t(kTileCols), features - c0));
     if (ct != loaded) {
@@ -309,6 +312,7 @@ kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
       gx[row * features + c0 + lane] = acc;
     }
     __syncwarp();
+    if (++rt == row_tiles) { rt = 0; ++ct; }
   }
 }
 
