@@ -876,59 +876,6 @@ bool pairs_enabled() {
   return on;
 }
 
-template <int kMode, int kF, int kPair>
-int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int64_t k,
-                const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& h,
-                GemmArgs args, int device, cudaStream_t stream, int* grid_out) {
-  auto kernel = kat_gemm_kernel<kMode, kF, kPair>;
-  constexpr uint32_t smem = smem_bytes<kMode, kPair>();
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
-      cudaSuccess)
-    return KAT_ERR_CUDA;
-  CUtensorMap mb;
-  if (!make_map(&mb, b, n, k, kBK, uint32_t(kBN / kPair), CU_TENSOR_MAP_SWIZZLE_128B))
-    return KAT_ERR_CUDA;
-  const char* stall = getenv("KAT_GEMM_TEST_STALL");
-  args.stall = (stall != nullptr && stall[0] == '1') ? 1 : 0;
-  args.m_tiles = int32_t((m + kBM * kPair - 1) / (kBM * kPair));
-  args.num_tiles = int32_t(int64_t(args.m_tiles) * (n / kBN));
-  const int sms = sm_count(device);
-  if (sms <= 0) return KAT_ERR_CUDA;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  cfg.blockDim = dim3(threads_of<kMode>());
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  int slots = sms;
-  if constexpr (kPair == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    static std::mutex mu;
-    static int cache[64] = {0};
-    std::lock_guard<std::mutex> lock(mu);
-    if (device < 0 || device >= 64) return KAT_ERR_CUDA;
-    if (cache[device] == 0) {
-      cfg.gridDim = dim3(2 * (sms / 2));
-      int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
-        clusters = -1;
-      cache[device] = clusters;
-    }
-    if (cache[device] < 0) return KAT_ERR_CUDA;
-    slots = cache[device];
-  }
-  if (slots > args.num_tiles) slots = args.num_tiles;
-  cfg.gridDim = dim3(uint32_t(slots * kPair));
-  if (cudaLaunchKernelEx(&cfg, kernel, ma, mb, o0, o1, h, args) != cudaSuccess)
-    return KAT_ERR_CUDA;
-  *grid_out = slots * kPair;
-  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
-}
-
 // Resident CTA pairs for this kernel on `device` (cluster occupancy, cached), or -1.
 template <int kMode, int kF>
 int pair_slots(int device) {
@@ -960,6 +907,48 @@ int pair_slots(int device) {
     cache[device] = clusters;
   }
   return cache[device];
+}
+
+template <int kMode, int kF, int kPair>
+int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int64_t k,
+                const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& h,
+                GemmArgs args, int device, cudaStream_t stream, int* grid_out) {
+  auto kernel = kat_gemm_kernel<kMode, kF, kPair>;
+  constexpr uint32_t smem = smem_bytes<kMode, kPair>();
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess)
+    return KAT_ERR_CUDA;
+  CUtensorMap mb;
+  if (!make_map(&mb, b, n, k, kBK, uint32_t(kBN / kPair), CU_TENSOR_MAP_SWIZZLE_128B))
+    return KAT_ERR_CUDA;
+  const char* stall = getenv("KAT_GEMM_TEST_STALL");
+  args.stall = (stall != nullptr && stall[0] == '1') ? 1 : 0;
+  args.m_tiles = int32_t((m + kBM * kPair - 1) / (kBM * kPair));
+  args.num_tiles = int32_t(int64_t(args.m_tiles) * (n / kBN));
+  const int sms = sm_count(device);
+  if (sms <= 0) return KAT_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(threads_of<kMode>());
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  int slots = sms;
+  if constexpr (kPair == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    slots = pair_slots<kMode, kF>(device);
+    if (slots < 1) return KAT_ERR_CUDA;
+  }
+  if (slots > args.num_tiles) slots = args.num_tiles;
+  cfg.gridDim = dim3(uint32_t(slots * kPair));
+  if (cudaLaunchKernelEx(&cfg, kernel, ma, mb, o0, o1, h, args) != cudaSuccess)
+    return KAT_ERR_CUDA;
+  *grid_out = slots * kPair;
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
 
 // One CTA pair per 256-row tile when that takes no more waves of tiles than one CTA per
