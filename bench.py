@@ -282,6 +282,10 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+# DRAM bytes per backward launch from the committed ncu capture of the same kernel and workload.
+NCU_BWD_TRAFFIC = {"kat_group_vitb_bf16": 309_910_272 + 123_047_168}
+
+
 def run_ours(args):
     import rational_kat_cu_b200 as kat
     from rational_kat_cu_b200 import distributed as kdist
@@ -518,7 +522,13 @@ def run_ours(args):
             "roofline": {
                 "bound": "hbm", "kernel": bwd_kernel_name,
                 "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
-                "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": NCU_BWD_TRAFFIC.get(w.name),
+                "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                   "kat_bwd_async_kernel launch, profiles/"
+                                   "kat_bwd_async_kernel_kat_group_vitb_bf16.md (writes still in "
+                                   "L2 at kernel end are not counted)")
+                if w.name in NCU_BWD_TRAFFIC else None,
                 "algorithmic_bytes_per_launch": 3 * N * elem_bytes,
                 "ms_per_launch": bwd_ms,
             },
@@ -1279,7 +1289,11 @@ def run_kan_mlp(args):
             "roofline": {"bound": "tensor", "kernel": "kat_gemm_kernel<1, 0> (fc1 + act2 forward)",
                          "achieved": flops_gemm / (f_ms * 1e-3) / 1e12, "peak": peak_tf[0],
                          "unit": "TFLOP/s", "frac": flops_gemm / (f_ms * 1e-3) / 1e12 / peak_tf[0],
-                         "peak_source": peak_tf[1], "traffic": None,
+                         "peak_source": peak_tf[1],
+                         "traffic": 120_227_584 + 259_228_672,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of "
+                                           "one kat_gemm_kernel<1, 0, 1> launch at this shape, "
+                                           "profiles/kat_gemm_kernel_kan_mlp_b16.md",
                          "algorithmic_flops_per_launch": flops_gemm, "ms_per_launch": f_ms},
             "kernels": {"fused_fwd_ms": f_ms, "fused_bwd_ms": b_ms, "plain_gemm_ms": p_ms,
                         "cublas_fc1_ms": c_ms,
