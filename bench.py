@@ -81,9 +81,11 @@ def parse_args():
                     help="how the ViT step exchanges the KAT coefficient gradients")
     ap.add_argument("--vit-eager", action="store_true",
                     help="eager ViT steps on one GPU instead of the captured CUDA graph")
-    ap.add_argument("--vit-fused-gemm", action="store_true",
+    ap.add_argument("--vit-fused-gemm", dest="vit_fused_gemm", action="store_true", default=True,
                     help="ViT: KAN blocks run fc1 -> act2 -> fc2 on the tcgen05 GEMMs with act2 "
-                         "in their epilogues")
+                         "in their epilogues (default)")
+    ap.add_argument("--vit-unfused-gemm", dest="vit_fused_gemm", action="store_false",
+                    help="ViT: KAN blocks on torch linear layers + the KAT_Group kernels")
     ap.add_argument("--vit-compare", action="store_true",
                     help="also time the ViT step with the reference's PyTorch KAT formulation "
                          "and with plain GELU MLPs (one GPU)")
