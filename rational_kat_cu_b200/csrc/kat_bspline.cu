@@ -3,8 +3,8 @@
 //
 // Work split: a block of 256 threads takes tiles of 8 batch rows x 32 features (warp w = row w,
 // lane = feature), walking the tiles of one 32-feature column before the next, so it keeps
-// those 32 features' knots in shared memory together with the correctly rounded reciprocals
-// of every knot difference the recursion divides by (1 / max(t_{j+k} - t_j, 1e-8), per
+// those 32 features' knots in shared memory together with every clamped knot difference the
+// recursion divides by, max(t_{j+k} - t_j, 1e-8), and its correctly rounded reciprocal (per
 // feature, level k and index j).
 //
 // Per element, instead of running the recursion over every knot interval (the reference
@@ -50,81 +50,119 @@ __device__ __forceinline__ float div_by(float a, float b, float y) {
   return __fmaf_rn(r, y, q0);
 }
 
-// Shared-memory layout of one column of tiles.
-// Knots and reciprocals are stored feature-minor ([index][32 features]): lane c reads
-// word index * 32 + c, in its own bank whatever index it needs, so the data-dependent span
-// lookups never conflict.
+// Shared-memory layout of one column of tiles, feature-minor ([index][32 features]): lane c
+// reads word index * 32 + c, in its own bank whatever index it needs, so the data-dependent
+// span lookups never conflict.  The tables are padded by kOrder entries so that every index a
+// span needs is in range without clamping:
+//   knots  [n_knots + 2 kOrder][32]   row j + kOrder holds t_{clamp(j, 0, n - 1)}
+//   recip  [kOrder][n_knots + kOrder][32]   row (k - 1, j + kOrder): 1 / max(t_{j+k} - t_j, eps)
+//   diff   [kOrder][n_knots + kOrder][32]   row (k - 1, j + kOrder): max(t_{j+k} - t_j, eps)
+// (recip and diff are 0 / 1 where j < 0 or j + k > n - 1: never read by a valid term).
 struct Smem {
-  float* knots;   // [n_knots][32]
-  float* recip;   // [kOrder][n_knots][32]: 1 / max(t_{j+k} - t_j, eps) at [k - 1][j][c]
+  float* knots;
+  float* recip;
+  float* diff;
   float* slab;    // [8][32 * n_basis]
 };
 
 size_t smem_bytes(int n_knots, int order) {
   const int nb = n_knots - 1 - order;
-  return sizeof(float) * (size_t(kTileCols) * n_knots + size_t(kTileCols) * order * n_knots +
-                          size_t(kTileRows) * kTileCols * nb);
+  return sizeof(float) * kTileCols *
+         (size_t(n_knots + 2 * order) + 2 * size_t(order) * (n_knots + order) +
+          size_t(kTileRows) * nb);
 }
 
-// Load the knots of features c0 .. c0 + 31 and tabulate the reciprocals.
+template <int kOrder>
+__host__ __device__ constexpr int table_rows(int n_knots) {
+  return n_knots + kOrder;
+}
+
+template <int kOrder>
+__device__ __forceinline__ Smem carve(float* smem, int n_knots) {
+  const int kr = n_knots + 2 * kOrder, tr = table_rows<kOrder>(n_knots);
+  Smem sm;
+  sm.knots = smem;
+  sm.recip = sm.knots + kTileCols * kr;
+  sm.diff = sm.recip + kTileCols * kOrder * tr;
+  sm.slab = sm.diff + kTileCols * kOrder * tr;
+  return sm;
+}
+
+// Load the knots of features c0 .. c0 + 31 and tabulate the clamped differences and their
+// correctly rounded reciprocals.
 template <int kOrder>
 __device__ __forceinline__ void load_column(const Smem& sm, const float* __restrict__ grid,
                                             int64_t features, int n_knots, int64_t c0) {
   const int ncols = int(min(int64_t(kTileCols), features - c0));
-  for (int q = threadIdx.x; q < kTileCols * n_knots; q += kBsThreads) {
-    const int c = q % kTileCols, j = q / kTileCols;
+  const int kr = n_knots + 2 * kOrder, tr = table_rows<kOrder>(n_knots);
+  for (int q = threadIdx.x; q < kTileCols * kr; q += kBsThreads) {
+    const int c = q % kTileCols, row = q / kTileCols;
+    const int j = min(max(row - kOrder, 0), n_knots - 1);
     sm.knots[q] = c < ncols ? grid[(c0 + c) * n_knots + j] : 0.0f;
   }
   __syncthreads();
-  for (int q = threadIdx.x; q < kTileCols * kOrder * n_knots; q += kBsThreads) {
+  const float* t = sm.knots + kTileCols * kOrder;  // t_j at t[j * 32 + c]
+  for (int q = threadIdx.x; q < kTileCols * kOrder * tr; q += kBsThreads) {
     const int c = q % kTileCols, kj = q / kTileCols;
-    const int k = kj / n_knots + 1, j = kj - (k - 1) * n_knots;
-    float v = 0.0f;
-    if (j + k < n_knots)
-      v = __frcp_rn(fmaxf(__fsub_rn(sm.knots[(j + k) * kTileCols + c],
-                                    sm.knots[j * kTileCols + c]), kEps));
-    sm.recip[q] = v;
+    const int k = kj / tr + 1, j = kj - (k - 1) * tr - kOrder;
+    float y = 0.0f, d = 1.0f;
+    if (j >= 0 && j + k < n_knots) {
+      d = fmaxf(__fsub_rn(t[(j + k) * kTileCols + c], t[j * kTileCols + c]), kEps);
+      y = __frcp_rn(d);
+    }
+    sm.recip[q] = y;
+    sm.diff[q] = d;
   }
   __syncthreads();
 }
 
-// Largest i in [0, n - 2] with t_i <= x, for t_0 <= x < t_{n-1} (non-decreasing t); knot t_j
-// of this lane's feature is t[j * 32].
+// Largest i in [0, n - 2] with t_i <= x, for t_0 <= x < t_{n-1} (non-decreasing t), by binary
+// search over the bits of i (a fixed number of steps, no data-dependent branches); knot t_j of
+// this lane's feature is t[j * 32].
 __device__ __forceinline__ int find_span(const float* t, int n, float x) {
-  int lo = 0, hi = n - 1;  // invariant: t_lo <= x < t_hi
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (t[mid * kTileCols] <= x) lo = mid; else hi = mid;
+  int i = 0;
+  for (int step = 1 << (31 - __clz(n - 2)); step > 0; step >>= 1) {
+    const int c = i + step;
+    if (c <= n - 2 && t[c * kTileCols] <= x) i = c;
   }
-  return lo;
+  return i;
 }
 
-// The knots t[i - kOrder .. i + kOrder + 1] of span i (w[q] = t[i - kOrder + q]) and, per level
-// k, the reciprocals 1 / max(t_{j+k} - t_j, eps) for j = i - k + 1 .. i (rw[k - 1][m - 1], m =
-// 1..k): everything the triangle reads, moved from shared memory to registers once.  Indices
-// outside the knot vector are clamped; those values are never used (see span_basis).
+// Everything the triangle of span i reads, moved from shared memory to registers once:
+// xl[q] = x - t_{i-kOrder+1+q}, xr[q] = t_{i+1+q} - x (q = 0 .. kOrder - 1), and per level k the
+// reciprocals and clamped differences of j = i - k + 1 .. i (rw / dw[k - 1][j - (i - k + 1)]).
+// kt points at this lane's padded knots (row j + kOrder = t_j), rc / df at its padded tables.
 template <int kOrder>
-__device__ __forceinline__ void load_span(const float* t, const float* rc, int n, int i,
-                                          float (&w)[2 * kOrder + 2],
-                                          float (&rw)[kOrder][kOrder]) {
+__device__ __forceinline__ void load_span(const float* kt, const float* rc, const float* df,
+                                          int n, int i, float x, float (&xl)[kOrder],
+                                          float (&xr)[kOrder], float (&rw)[kOrder][kOrder],
+                                          float (&dw)[kOrder][kOrder]) {
+  const int tr = table_rows<kOrder>(n);
 #pragma unroll
-  for (int q = 0; q < 2 * kOrder + 2; ++q)
-    w[q] = t[min(max(i - kOrder + q, 0), n - 1) * kTileCols];
+  for (int q = 0; q < kOrder; ++q) {
+    xl[q] = __fsub_rn(x, kt[(i + 1 + q) * kTileCols]);               // t_{i-kOrder+1+q}
+    xr[q] = __fsub_rn(kt[(i + 1 + q + kOrder) * kTileCols], x);      // t_{i+1+q}
+  }
 #pragma unroll
   for (int k = 1; k <= kOrder; ++k) {
 #pragma unroll
-    for (int m = 1; m <= k; ++m)
-      rw[k - 1][m - 1] = rc[((k - 1) * n + max(i - k + m, 0)) * kTileCols];
+    for (int m = 0; m < k; ++m) {
+      const int row = (k - 1) * tr + (i - k + 1 + m + kOrder);
+      rw[k - 1][m] = rc[row * kTileCols];
+      dw[k - 1][m] = df[row * kTileCols];
+    }
   }
 }
 
 // Basis values of order kOrder that can be non-zero at x in span i: b[m] = B^kOrder_{i-kOrder+m}
 // for m = 0..kOrder (entries whose index is outside [0, n - 2 - kOrder] are left 0), and, when
-// kGrad, their derivatives db[m].  Knot t_j is w[j - i + kOrder].
+// kGrad, their derivatives db[m].  Each term is ((numerator / clamped difference) x the lower
+// order value), the two terms added without a fused multiply-add, as the reference's recursion.
 template <int kOrder, bool kGrad>
-__device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2],
-                                           const float (&rw)[kOrder][kOrder], int n, int i,
-                                           float x, float (&b)[kMaxOrder + 1],
+__device__ __forceinline__ void span_basis(const float (&xl)[kOrder], const float (&xr)[kOrder],
+                                           const float (&rw)[kOrder][kOrder],
+                                           const float (&dw)[kOrder][kOrder], int n, int i,
+                                           float (&b)[kMaxOrder + 1],
                                            float (&db)[kMaxOrder + 1]) {
   float prev[kMaxOrder + 1], dprev[kMaxOrder + 1];
   prev[0] = 1.0f;
@@ -134,15 +172,14 @@ __device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2],
 #pragma unroll
     for (int m = 0; m <= k; ++m) {
       const int j = i - k + m;
-      const int o = kOrder - k + m;  // position of t_j in the window
       float v = 0.0f, dv = 0.0f;
       if (j >= 0 && j <= n - 2 - k) {
         // left term: (x - t_j) / max(t_{j+k} - t_j, eps) * B^{k-1}_j   (prev index m - 1)
         float left = 0.0f, dleft = 0.0f;
         if (m >= 1) {
-          const float d1 = fmaxf(__fsub_rn(w[o + k], w[o]), kEps);
+          const float d1 = dw[k - 1][m - 1];
           const float y1 = rw[k - 1][m - 1];
-          const float u = div_by(__fsub_rn(x, w[o]), d1, y1);
+          const float u = div_by(xl[kOrder - 1 - k + m], d1, y1);
           left = __fmul_rn(u, prev[m - 1]);
           if constexpr (kGrad)
             dleft = __fadd_rn(div_by(prev[m - 1], d1, y1), __fmul_rn(u, dprev[m - 1]));
@@ -150,9 +187,9 @@ __device__ __forceinline__ void span_basis(const float (&w)[2 * kOrder + 2],
         // right term: (t_{j+k+1} - x) / max(t_{j+k+1} - t_{j+1}, eps) * B^{k-1}_{j+1}   (m)
         float right = 0.0f, dright = 0.0f;
         if (m <= k - 1) {
-          const float d2 = fmaxf(__fsub_rn(w[o + k + 1], w[o + 1]), kEps);
+          const float d2 = dw[k - 1][m];
           const float y2 = rw[k - 1][m];
-          const float r = div_by(__fsub_rn(w[o + k + 1], x), d2, y2);
+          const float r = div_by(xr[m], d2, y2);
           right = __fmul_rn(r, prev[m]);
           if constexpr (kGrad)
             dright = __fsub_rn(__fmul_rn(r, dprev[m]), div_by(prev[m], d2, y2));
@@ -212,7 +249,7 @@ kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
                        float* __restrict__ out, int64_t batch, int64_t features, int n_knots) {
   extern __shared__ __align__(16) float smem[];
   const int nb = n_knots - 1 - kOrder;
-  const Smem sm{smem, smem + kTileCols * n_knots, smem + kTileCols * n_knots * (1 + kOrder)};
+  const Smem sm = carve<kOrder>(smem, n_knots);
   const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
   const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
   int64_t t0, t1;
@@ -237,16 +274,17 @@ kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
     __syncwarp();
     if (row < batch && lane < ncols) {
       const float v = x[row * features + c0 + lane];
-      const float* t = sm.knots + lane;
+      const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
       float* r = srow + lane * nb;
       if (!isfinite(v)) {
         for (int j = 0; j < nb; ++j) r[j] = __int_as_float(0x7fc00000);
       } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
         const int i = find_span(t, n_knots, v);
-        float w[2 * kOrder + 2], rw[kOrder][kOrder];
-        load_span<kOrder>(t, sm.recip + lane, n_knots, i, w, rw);
+        float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
+        load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
+                          xr, rw, dw);
         float b[kMaxOrder + 1], db[kMaxOrder + 1];
-        span_basis<kOrder, false>(w, rw, n_knots, i, v, b, db);
+        span_basis<kOrder, false>(xl, xr, rw, dw, n_knots, i, b, db);
 #pragma unroll
         for (int m = 0; m <= kOrder; ++m) {
           const int j = i - kOrder + m;
@@ -268,7 +306,7 @@ kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
                        int64_t features, int n_knots) {
   extern __shared__ __align__(16) float smem[];
   const int nb = n_knots - 1 - kOrder;
-  const Smem sm{smem, smem + kTileCols * n_knots, smem + kTileCols * n_knots * (1 + kOrder)};
+  const Smem sm = carve<kOrder>(smem, n_knots);
   const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
   const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
   int64_t t0, t1;
@@ -292,17 +330,18 @@ kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
     __syncwarp();
     if (row < batch && lane < ncols) {
       const float v = x[row * features + c0 + lane];
-      const float* t = sm.knots + lane;
+      const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
       const float* r = srow + lane * nb;
       float acc = 0.0f;
       if (!isfinite(v)) {
         acc = __int_as_float(0x7fc00000);
       } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
         const int i = find_span(t, n_knots, v);
-        float w[2 * kOrder + 2], rw[kOrder][kOrder];
-        load_span<kOrder>(t, sm.recip + lane, n_knots, i, w, rw);
+        float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
+        load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
+                          xr, rw, dw);
         float b[kMaxOrder + 1], db[kMaxOrder + 1];
-        span_basis<kOrder, true>(w, rw, n_knots, i, v, b, db);
+        span_basis<kOrder, true>(xl, xr, rw, dw, n_knots, i, b, db);
 #pragma unroll
         for (int m = 0; m <= kOrder; ++m) {
           const int j = i - kOrder + m;
