@@ -44,8 +44,11 @@ int kat_bspline_basis_fwd(const float* x, const float* grid, float* bases,
  * Backward: grad_x[b, d] = sum_j grad_bases[b, d, j] * d B_j / dx (x[b, d]), the derivative
  * torch autograd takes through the recursion above (the indicator functions contribute
  * nothing; each term contributes +-B^{k-1} / clamped difference plus its factor times the
- * lower-order derivative).  Replaces rational_kat_cu/bspline_basis.py:562-599
- * (bspline_basis_bwd).  The grid gets no gradient, as in the reference.
+ * lower-order derivative), evaluated with the B-spline derivative identity
+ * dB^K_j/dx = K (B^{K-1}_j / max(t_{j+K} - t_j, 1e-8) - B^{K-1}_{j+1} / max(t_{j+K+1} - t_{j+1}, 1e-8)),
+ * which equals that autograd value up to rounding.  Replaces
+ * rational_kat_cu/bspline_basis.py:562-599 (bspline_basis_bwd).  The grid gets no gradient, as in
+ * the reference.
  */
 int kat_bspline_basis_bwd(const float* x, const float* grid, const float* grad_bases,
                           float* grad_x, int64_t batch, int64_t features, int32_t n_knots,

@@ -18,8 +18,12 @@
 // q0 = RN(a y), r = a - b q0 (exact, one FMA), q = RN(q0 + r y), which is the correctly
 // rounded quotient RN(a / b) (P. Markstein, "Computation of elementary functions on the IBM
 // RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990) — the IEEE division result at
-// three FP32 operations.  Outputs (forward) and incoming gradients (backward) go through
-// shared memory so each row of a tile moves as one contiguous, coalesced range.
+// three FP32 operations.  The backward takes the derivative from the order K - 1 values with
+// the B-spline identity dB^K_j/dx = K (B^{K-1}_j / d^K_j - B^{K-1}_{j+1} / d^K_{j+1}) (d the
+// clamped knot differences), which equals the derivative autograd takes through the recursion
+// up to rounding, at the cost of the forward recursion to order K - 1.  Outputs (forward) and
+// incoming gradients (backward) go through shared memory so each row of a tile moves as one
+// contiguous, coalesced range.
 //
 // Knots must be non-decreasing along each feature (KANLinear's grid and update_grid produce
 // such grids).  A non-finite x gives NaN in every basis value, as the reference's full
@@ -154,58 +158,42 @@ __device__ __forceinline__ void load_span(const float* kt, const float* rc, cons
   }
 }
 
-// Basis values of order kOrder that can be non-zero at x in span i: b[m] = B^kOrder_{i-kOrder+m}
-// for m = 0..kOrder (entries whose index is outside [0, n - 2 - kOrder] are left 0), and, when
-// kGrad, their derivatives db[m].  Each term is ((numerator / clamped difference) x the lower
+// Basis values of order kLevels (<= kOrder) that can be non-zero at x in span i:
+// b[m] = B^kLevels_{i-kLevels+m} for m = 0..kLevels (entries whose index is outside
+// [0, n - 2 - kLevels] are left 0).  Each term is ((numerator / clamped difference) x the lower
 // order value), the two terms added without a fused multiply-add, as the reference's recursion.
-template <int kOrder, bool kGrad>
+// The windows are those load_span<kOrder> filled.
+template <int kOrder, int kLevels>
 __device__ __forceinline__ void span_basis(const float (&xl)[kOrder], const float (&xr)[kOrder],
                                            const float (&rw)[kOrder][kOrder],
                                            const float (&dw)[kOrder][kOrder], int n, int i,
-                                           float (&b)[kMaxOrder + 1],
-                                           float (&db)[kMaxOrder + 1]) {
-  float prev[kMaxOrder + 1], dprev[kMaxOrder + 1];
+                                           float (&b)[kMaxOrder + 1]) {
+  float prev[kMaxOrder + 1];
   prev[0] = 1.0f;
-  dprev[0] = 0.0f;
 #pragma unroll
-  for (int k = 1; k <= kOrder; ++k) {
+  for (int k = 1; k <= kLevels; ++k) {
 #pragma unroll
     for (int m = 0; m <= k; ++m) {
       const int j = i - k + m;
-      float v = 0.0f, dv = 0.0f;
+      float v = 0.0f;
       if (j >= 0 && j <= n - 2 - k) {
         // left term: (x - t_j) / max(t_{j+k} - t_j, eps) * B^{k-1}_j   (prev index m - 1)
-        float left = 0.0f, dleft = 0.0f;
-        if (m >= 1) {
-          const float d1 = dw[k - 1][m - 1];
-          const float y1 = rw[k - 1][m - 1];
-          const float u = div_by(xl[kOrder - 1 - k + m], d1, y1);
-          left = __fmul_rn(u, prev[m - 1]);
-          if constexpr (kGrad)
-            dleft = __fadd_rn(div_by(prev[m - 1], d1, y1), __fmul_rn(u, dprev[m - 1]));
-        }
+        float left = 0.0f;
+        if (m >= 1)
+          left = __fmul_rn(div_by(xl[kOrder - 1 - k + m], dw[k - 1][m - 1], rw[k - 1][m - 1]),
+                           prev[m - 1]);
         // right term: (t_{j+k+1} - x) / max(t_{j+k+1} - t_{j+1}, eps) * B^{k-1}_{j+1}   (m)
-        float right = 0.0f, dright = 0.0f;
-        if (m <= k - 1) {
-          const float d2 = dw[k - 1][m];
-          const float y2 = rw[k - 1][m];
-          const float r = div_by(xr[m], d2, y2);
-          right = __fmul_rn(r, prev[m]);
-          if constexpr (kGrad)
-            dright = __fsub_rn(__fmul_rn(r, dprev[m]), div_by(prev[m], d2, y2));
-        }
+        float right = 0.0f;
+        if (m <= k - 1)
+          right = __fmul_rn(div_by(xr[m], dw[k - 1][m], rw[k - 1][m]), prev[m]);
         v = __fadd_rn(left, right);
-        if constexpr (kGrad) dv = __fadd_rn(dleft, dright);
       }
       b[m] = v;
-      db[m] = dv;
     }
 #pragma unroll
-    for (int m = 0; m <= k; ++m) {
-      prev[m] = b[m];
-      dprev[m] = db[m];
-    }
+    for (int m = 0; m <= k; ++m) prev[m] = b[m];
   }
+  if constexpr (kLevels == 0) b[0] = 1.0f;
 }
 
 // Warp-wide copy of `count` floats between a tile row's slab (16-byte aligned) and global
@@ -283,8 +271,8 @@ kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
         float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
         load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
                           xr, rw, dw);
-        float b[kMaxOrder + 1], db[kMaxOrder + 1];
-        span_basis<kOrder, false>(xl, xr, rw, dw, n_knots, i, b, db);
+        float b[kMaxOrder + 1];
+        span_basis<kOrder, kOrder>(xl, xr, rw, dw, n_knots, i, b);
 #pragma unroll
         for (int m = 0; m <= kOrder; ++m) {
           const int j = i - kOrder + m;
@@ -340,12 +328,20 @@ kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ gr
         float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
         load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
                           xr, rw, dw);
-        float b[kMaxOrder + 1], db[kMaxOrder + 1];
-        span_basis<kOrder, true>(xl, xr, rw, dw, n_knots, i, b, db);
+        // dB^K_j / dx = K (B^{K-1}_j / d_j - B^{K-1}_{j+1} / d_{j+1}), d_j = max(t_{j+K} - t_j,
+        // eps): the derivative autograd takes through the recursion, from the order K - 1 values
+        // (b[m'] = B^{K-1}_{i-K+1+m'}) and the level-K reciprocals.
+        float b[kMaxOrder + 1];
+        span_basis<kOrder, kOrder - 1>(xl, xr, rw, dw, n_knots, i, b);
 #pragma unroll
         for (int m = 0; m <= kOrder; ++m) {
           const int j = i - kOrder + m;
-          if (j >= 0 && j < nb) acc = __fadd_rn(acc, __fmul_rn(r[j], db[m]));
+          if (j >= 0 && j < nb) {
+            const float left = m >= 1 ? __fmul_rn(b[m - 1], rw[kOrder - 1][m - 1]) : 0.0f;
+            const float right = m <= kOrder - 1 ? __fmul_rn(b[m], rw[kOrder - 1][m]) : 0.0f;
+            const float d = __fmul_rn(float(kOrder), __fsub_rn(left, right));
+            acc = __fadd_rn(acc, __fmul_rn(r[j], d));
+          }
         }
       }
       gx[row * features + c0 + lane] = acc;
