@@ -1171,7 +1171,7 @@ def run_kan_mlp_reference(args):
     rate, info = _kan_cpu_rate(args.cpu_seconds, steps=steps, warmup=warm)
     print(json.dumps({
         "impl": "reference", "metric": KAN_METRIC, "value": rate, "unit": KAN_UNIT,
-        "n_gpus": 0, "steps": steps, "warmup": warm, "ms_per_step": info["seconds_per_step"] * 1e3,
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": info["seconds_per_step"] * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": KAN_WORKLOAD, "tokens": info["tokens"]},
         "cpu_baseline": {"value": rate, "unit": KAN_UNIT, "cores": info["cores"], "kind": "port",
