@@ -42,6 +42,7 @@ import torch  # noqa: E402
 METRIC = "KAT_Group fwd+bwd Gelem/s"
 UNIT = "Gelem/s"
 FALLBACK_HBM_GBS = 6650.0
+SPEC_HBM_GBS = 8000.0          # the ~8 TB/s HBM3e figure the fractions are also quoted against
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -69,9 +70,18 @@ def parse_args():
     ap.add_argument("--e2e-chunks", type=int, default=16,
                     help="row chunks the host-buffer pipeline overlaps")
     ap.add_argument("--kernel-iters", type=int, default=100)
-    ap.add_argument("--cpu-seconds", type=float, default=12.0,
-                    help="CPU budget of the reference-path baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=30.0,
+                    help="CPU budget of our line's reference-path baseline (median of 5 steps "
+                         "after one warm-up, full batch when it fits the budget)")
+    ap.add_argument("--ref-seconds", type=float, default=300.0,
+                    help="CPU budget of the whole --impl reference run (full batch per step "
+                         "when (steps + warmup) full steps fit, else a row sample)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-gpu-bar", action="store_true",
+                    help="do not time the reference's Triton kernels on this GPU")
+    ap.add_argument("--skip-2d", action="store_true",
+                    help="do not time the KAT_Group2D workload beside the headline")
+    ap.add_argument("--gpu-bar-child", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--sweep", action="store_true",
                     help="print one line per bandwidth-sweep point (kernel timings) instead")
     ap.add_argument("--vit-batch", type=int, default=128,
@@ -191,9 +201,26 @@ class ClockSampler:
 # CPU baseline: the reference's CPU path (oracle restatement) on a bounded sample
 # ---------------------------------------------------------------------------
 
-def cpu_reference_rate(workload, budget_s: float, steps: int = 0, warmup: int = 0):
-    """Time fwd+bwd of the reference's PyTorch CPU path (restated in oracle/) on a sample of
-    `workload` rows.  Returns (Gelem/s, dict describing the sample)."""
+def workload_config(w):
+    """The `config` both arms print for workload `w` (identical, so the two lines compare)."""
+    eb = {"f32": 4, "bf16": 2, "f16": 2}[w.dtype]
+    tensor = w.numel * eb
+    return {
+        "workload": w.name, "shape": list(w.shape), "num_groups": w.groups, "io_dtype": w.dtype,
+        "coefficients": "gelu + N(0,0.01)" if w.perturb else w.mode,
+        "formula": "abs-after-sum (rat_cuda)" if w.formula == 1 else "KAT (kat_1dgroup_torch)",
+        "layout": w.layout, "elements_per_gpu": w.numel,
+        "l2": (f"inputs larger than L2 ({tensor / 1e6:.0f} MB per tensor > {L2_BYTES / 1e6:.0f} MB)"
+               if tensor > L2_BYTES else "inputs fit in L2"),
+    }
+
+
+def cpu_reference_rate(workload, budget_s: float, steps: int = 5, warmup: int = 1):
+    """Time fwd+bwd of the reference's PyTorch CPU path (restated in oracle/) on `workload`:
+    `warmup` untimed steps, then `steps` timed ones; the rate is elements per step over the
+    median step time.  Each step covers the full batch when (steps + warmup) full steps fit in
+    `budget_s` (estimated from one row), else the largest row sample that does.  Returns
+    (Gelem/s, dict describing the sample)."""
     from oracle import kat_torch_oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -227,24 +254,29 @@ def cpu_reference_rate(workload, budget_s: float, steps: int = 0, warmup: int = 
     t0 = time.perf_counter()
     one(x, gy)
     per_row = max(time.perf_counter() - t0, 1e-4)
-    n_calls = (steps + warmup) if steps else 3
-    rows = int(max(1, min(shape[0], budget_s / max(n_calls, 1) / per_row)))
+    steps = max(1, steps)
+    n_calls = steps + warmup
+    rows = int(max(1, min(shape[0], budget_s / n_calls / per_row)))
     x, gy = make(rows)
-    for _ in range(warmup if steps else 1):
+    for _ in range(warmup):
         one(x, gy)
-    reps = steps if steps else 2
-    t0 = time.perf_counter()
-    for _ in range(reps):
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
         one(x, gy)
-    dt = (time.perf_counter() - t0) / reps
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
     elems = rows * row_elems
+    full = rows == shape[0]
     return elems / dt / 1e9, {
-        "cores": cores, "rows": rows, "elements": elems, "seconds_per_step": dt, "reps": reps,
-        "sample": f"x[{rows},{','.join(str(s) for s in shape[1:])}] of {workload.name} "
-                  f"(fp32 upcast), fwd+bwd"
-                  + (" (rat_cuda formula, the reference's PyTorch definition)"
-                     if workload.formula == 1 else "")
-                  + f", mean of {reps} timed steps"}
+        "cores": cores, "rows": rows, "full_batch": full, "elements": elems,
+        "seconds_per_step": dt, "steps": steps, "warmup": warmup,
+        "sample": (f"x[{rows},{','.join(str(s) for s in shape[1:])}] "
+                   + ("(the full batch)" if full else f"(a {rows}-row sample)")
+                   + f" of {workload.name} (fp32 upcast), fwd+bwd"
+                   + (" (rat_cuda formula, the reference's PyTorch definition)"
+                      if workload.formula == 1 else "")
+                   + f", median of {steps} timed steps after {warmup} warm-up")}
 
 
 def run_reference(args):
@@ -254,16 +286,16 @@ def run_reference(args):
     from rational_kat_cu_b200 import workloads
 
     w = workloads.get(args.workload)
-    rate, info = cpu_reference_rate(w, budget_s=min(150.0, 10.0 + 0.5 * (args.steps + args.warmup)),
-                                    steps=args.steps, warmup=args.warmup)
+    rate, info = cpu_reference_rate(w, budget_s=args.ref_seconds, steps=args.steps,
+                                    warmup=args.warmup)
     line = {
         "metric": metric_for(w), "value": rate, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": info["seconds_per_step"] * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": w.name, "shape": list(w.shape), "num_groups": w.groups,
-                   "sample_shape": [info["rows"]] + list(w.shape[1:])},
+        "config": workload_config(w),
+        "sample_rows": info["rows"], "full_batch": info["full_batch"],
         "cpu_baseline": {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
                          "sample": info["sample"]},
         "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -384,6 +416,21 @@ def run_ours(args):
     ms_per_step = ms_total / args.steps
     value = world * N / (ms_per_step * 1e-3) / 1e9
 
+    # The coefficient gradients of the last step on every rank, compared bit for bit.
+    grads = torch.cat([mod.weight_numerator.grad.reshape(-1).float(),
+                       mod.weight_denominator.grad.reshape(-1).float()]).contiguous()
+    grads_finite = bool(torch.isfinite(grads).all().item())
+    if dist is not None:
+        gathered = torch.empty(world, grads.numel(), device=dev, dtype=grads.dtype)
+        dist.all_gather_into_tensor(gathered, grads)
+        bits = gathered.view(torch.int32)
+        grads_identical = bool((bits == bits[0:1]).all().item())
+        fin = torch.tensor([1 if grads_finite else 0], device=dev)
+        dist.all_reduce(fin, op=dist.ReduceOp.MIN)
+        grads_finite = bool(fin.item())
+    else:
+        grads_identical = True
+
     # Kernel-level timing: back-to-back C-ABI launches on device-resident, preallocated
     # buffers (no Python work inside the loop beyond the call), CUDA events on the launching
     # stream around the whole run, average per launch.
@@ -493,9 +540,20 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
-        rate, info = cpu_reference_rate(w, budget_s=args.cpu_seconds)
+        rate, info = cpu_reference_rate(w, budget_s=args.cpu_seconds, steps=5, warmup=1)
         cpu = {"value": rate, "unit": UNIT, "cores": info["cores"], "kind": "port",
                "sample": info["sample"]}
+
+    # KAT_Group2D (x[64,256,56,56] fp32 NCHW, identity init) beside the headline, and the
+    # reference's own Triton kernels on this GPU as a throughput bar (one GPU only).
+    kat2d = None
+    if rank == 0 and world == 1 and not args.skip_2d and w.name == "kat_group_vitb_bf16":
+        kat2d = _kat2d_numbers(dev, stream, args)
+    gpu_bar = None
+    if rank == 0 and world == 1 and not args.skip_gpu_bar and w.formula == 0:
+        names = ["kat_group_vitb_bf16", "kat_group2d_f32"] if w.name == "kat_group_vitb_bf16" \
+            else [w.name]
+        gpu_bar = _gpu_bar(local, names)
 
     if dist is not None:
         dist.barrier()
@@ -507,24 +565,20 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": w.dtype, "data": "synthetic",
-            "config": {
-                "workload": w.name, "shape": list(w.shape), "num_groups": w.groups,
-                "coefficients": "gelu + N(0,0.01)" if w.perturb else w.mode,
-                "formula": "abs-after-sum (rat_cuda)" if formula == 1 else "KAT (kat_1dgroup_torch)",
-                "elements_per_gpu": N, "layout": w.layout,
-                "l2": f"inputs larger than L2 ({N * elem_bytes / 1e6:.0f} MB per tensor > "
-                      f"{L2_BYTES / 1e6:.0f} MB)",
-                "step": "module forward + backward" + (" in a CUDA graph" if graph else "")
-                        + (" with the coefficient-gradient exchange fused into the reduction "
-                           "kernel (NVLink peer stores)" if world > 1 and not eager_exchange
-                           else "")
-                        + (" and an NCCL all-gather of the coefficient gradients"
-                           if eager_exchange else ""),
-            },
+            "config": workload_config(w),
+            "step": "module forward + backward" + (" in a CUDA graph" if graph else "")
+                    + (" with the coefficient-gradient exchange fused into the reduction "
+                       "kernel (NVLink peer stores)" if world > 1 and not eager_exchange
+                       else "")
+                    + (" and an NCCL all-gather of the coefficient gradients"
+                       if eager_exchange else ""),
+            "nranks": world, "grads_identical": grads_identical, "grads_finite": grads_finite,
             "roofline": {
                 "bound": "hbm", "kernel": bwd_kernel_name,
                 "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
                 "peak_source": f"{peak_kind} hbm_gbs",
+                "frac_of_spec": bwd_gbs / SPEC_HBM_GBS,
+                "spec_gbs": SPEC_HBM_GBS,
                 "traffic": NCU_BWD_TRAFFIC.get(w.name),
                 "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                                    "kat_bwd_async_kernel launch, profiles/"
@@ -536,9 +590,17 @@ def run_ours(args):
             },
             "kernels": {
                 "fwd_ms": fwd_ms, "fwd_GBps": fwd_gbs, "fwd_frac": fwd_gbs / peak,
+                "fwd_frac_spec": fwd_gbs / SPEC_HBM_GBS,
                 "bwd_ms": bwd_ms, "bwd_GBps": bwd_gbs, "bwd_frac": bwd_gbs / peak,
+                "bwd_frac_spec": bwd_gbs / SPEC_HBM_GBS,
+                "step_GBps": step_bytes / (ms_per_step * 1e-3) / 1e9,
                 "step_hbm_frac": step_bytes * world / (ms_per_step * 1e-3) / 1e9 / (peak * world),
+                "step_hbm_frac_spec": step_bytes / (ms_per_step * 1e-3) / 1e9 / SPEC_HBM_GBS,
+                "fractions": f"of measured {peak:.0f} GB/s ({peak_kind}) and of the "
+                             f"{SPEC_HBM_GBS:.0f} GB/s spec (_spec)",
             },
+            "kat_group2d": kat2d,
+            "gpu_bar": gpu_bar,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms_step,
                     "api": f"rational_kat_cu_b200.host_io.HostPipeline ({args.e2e_chunks} "
@@ -552,8 +614,218 @@ def run_ours(args):
     if graph is not None:
         del graph
     if dist is not None:
+        if getattr(mod, "exchange", None) is not None:
+            mod.disable_data_parallel()       # collective: unmap, barrier, free
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _kat2d_numbers(dev, stream, args):
+    """KAT_Group2D over x[64,256,56,56] fp32 NCHW (identity init, G=8): module forward and
+    module forward + backward, each captured in a CUDA graph and timed over replays, and the
+    C-ABI forward / backward launches back to back; fractions of the HBM bytes 2s / 3s / 5s
+    per element against the measured peak and the spec figure."""
+    import ctypes
+
+    import rational_kat_cu_b200 as kat
+    from rational_kat_cu_b200 import _native, workloads
+
+    w = workloads.get("kat_group2d_f32")
+    N = w.numel
+    eb = 4
+    mod = kat.KAT_Group2D(num_groups=w.groups, mode=w.mode).to(dev)
+    x, gy = w.inputs(dev)
+    x.requires_grad_(True)
+    peak, _ = measured_peak()
+    reps = max(5, min(args.steps, 50))
+
+    def graphed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        torch.cuda.synchronize(dev)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            g.replay()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        del g
+        return a.elapsed_time(b) / reps
+
+    def fwd_only():
+        with torch.no_grad():
+            mod(x)
+
+    def fwd_bwd():
+        mod.zero_grad(set_to_none=False)
+        x.grad = None
+        mod(x).backward(gy)
+
+    mod_fwd_ms = graphed(fwd_only)
+    mod.zero_grad(set_to_none=True)
+    mod_step_ms = graphed(fwd_bwd)
+
+    lib = _native.lib()
+    dims = w.dims()
+    wn, wd = w.coefficients()
+    num = wn.repeat(w.groups, 1).to(dev).contiguous()
+    den = wd.to(dev).contiguous()
+    xs = x.detach()
+    y, dx = torch.empty_like(xs), torch.empty_like(xs)
+    dn = torch.empty(w.groups, 6, device=dev)
+    dd = torch.empty(w.groups, 4, device=dev)
+    need = ctypes.c_size_t(0)
+    _native.check("ws", lib.kat_rational_bwd_workspace_size(*dims, w.groups, _native.KAT_DTYPE_F32,
+                                                            dev.index, ctypes.byref(need)))
+    ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=dev)
+    sp = ctypes.c_void_p(stream.cuda_stream)
+    fa = (xs.data_ptr(), y.data_ptr(), num.data_ptr(), den.data_ptr(), *dims, w.groups,
+          _native.KAT_DTYPE_F32, sp)
+    ba = (xs.data_ptr(), gy.data_ptr(), dx.data_ptr(), num.data_ptr(), den.data_ptr(),
+          dn.data_ptr(), dd.data_ptr(), ws.data_ptr(), ws.numel(), *dims, w.groups,
+          _native.KAT_DTYPE_F32, sp)
+    out = []
+    for fn, a in ((lib.kat_rational_fwd, fa), (lib.kat_rational_bwd, ba)):
+        for _ in range(3):
+            _native.check("launch", fn(*a))
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.kernel_iters):
+            fn(*a)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        out.append(e0.elapsed_time(e1) / args.kernel_iters)
+    k_fwd, k_bwd = out
+
+    def gbs(nbytes, ms):
+        return nbytes / (ms * 1e-3) / 1e9
+
+    res = {
+        "workload": w.name, "shape": list(w.shape), "num_groups": w.groups, "io_dtype": "f32",
+        "coefficients": w.mode, "elements": N,
+        "module_fwd_ms": mod_fwd_ms, "module_fwd_bwd_ms": mod_step_ms,
+        "fwd_bwd_gelem_s": N / (mod_step_ms * 1e-3) / 1e9,
+        "kernel_fwd_ms": k_fwd, "kernel_bwd_ms": k_bwd,
+        "fwd_frac": gbs(2 * N * eb, k_fwd) / peak,
+        "fwd_frac_spec": gbs(2 * N * eb, k_fwd) / SPEC_HBM_GBS,
+        "bwd_frac": gbs(3 * N * eb, k_bwd) / peak,
+        "bwd_frac_spec": gbs(3 * N * eb, k_bwd) / SPEC_HBM_GBS,
+        "fwd_bwd_frac": gbs(5 * N * eb, mod_step_ms) / peak,
+        "fwd_bwd_frac_spec": gbs(5 * N * eb, mod_step_ms) / SPEC_HBM_GBS,
+        "timing": f"module steps in a CUDA graph, {reps} replays; C-ABI launches back to back, "
+                  f"{args.kernel_iters} per direction; CUDA events",
+    }
+    del mod, x, gy, y, dx, ws
+    torch.cuda.empty_cache()
+    return res
+
+
+def _gpu_bar(local, names):
+    """The reference's own Triton kernels (rational_fwd_triton / rational_bwd_triton and the
+    2D ones, from the reference installed under baseline/_ref) timed on this GPU at the given
+    workloads, in a child process so their package cannot shadow this repository's import
+    shims.  A throughput bar only: those kernels compute other denominator formulas."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "kat_rational")):
+        return {"kind": "reference_triton", "unavailable": "reference not installed under "
+                "baseline/_ref"}
+    env = dict(os.environ, LOCAL_RANK=str(local))
+    for k in ("RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        res = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--gpu-bar-child",
+                              ",".join(names)], env=env, capture_output=True, text=True,
+                             timeout=900, cwd=os.path.dirname(REPO))
+    except subprocess.TimeoutExpired:
+        return {"kind": "reference_triton", "unavailable": "timed out after 900 s"}
+    lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    if res.returncode != 0 or not lines:
+        tail = (res.stderr or res.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"kind": "reference_triton",
+                "unavailable": f"child exited {res.returncode}: {tail[0][:300]}"}
+    return json.loads(lines[-1])
+
+
+def run_gpu_bar_child(names):
+    """Child of _gpu_bar: imports the installed reference first on sys.path, then times its
+    Triton launchers with CUDA events (3 warm-up calls, which include the JIT compile, then
+    10 timed calls per direction)."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    sys.path[:] = [ref] + [p for p in sys.path
+                           if p not in ("", ".") and os.path.abspath(p) != REPO] + [REPO]
+    out = {"kind": "reference_triton",
+           "source": "kat_rational.rational_triton.rational_fwd_triton / rational_bwd_triton and "
+                     "rational_triton2d.rational_fwd_triton_2d / rational_bwd_triton_2d of the "
+                     "reference installed under baseline/_ref",
+           "formula_note": "throughput bar only: the reference's Triton forward uses "
+                           "Q = 1 + |sum b_i x^i| and its backward Q = 1 + sum |b_i||x|^i, not the "
+                           "PyTorch formula this repository implements; its backward adds 10 "
+                           "float atomics per element"}
+    try:
+        import kat_rational.rational_triton as rt
+        import kat_rational.rational_triton2d as rt2
+        import triton
+        if not os.path.abspath(rt.__file__).startswith(os.path.abspath(ref)):
+            raise ImportError(f"kat_rational resolved to {rt.__file__}")
+        out["triton"] = triton.__version__
+    except Exception as e:
+        out["unavailable"] = f"import failed: {type(e).__name__}: {e}"
+        print(json.dumps(out), flush=True)
+        return
+    from rational_kat_cu_b200 import workloads
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = measured_peak()
+    for name in names:
+        w = workloads.get(name)
+        eb = {"f32": 4, "bf16": 2, "f16": 2}[w.dtype]
+        x, gy = w.inputs(dev)
+        wn, wd = w.coefficients()
+        n = wn.repeat(w.groups, 1).to(dev).contiguous()
+        d = wd.to(dev).contiguous()
+        if w.layout == "nchw":
+            fwd = lambda: rt2.rational_fwd_triton_2d(x, n, d, w.groups)  # noqa: E731
+            bwd = lambda: rt2.rational_bwd_triton_2d(gy, x, n, d, w.groups)  # noqa: E731
+        else:
+            fwd = lambda: rt.rational_fwd_triton(x, n, d, w.groups)  # noqa: E731
+            bwd = lambda: rt.rational_bwd_triton(gy, x, n, d, w.groups)  # noqa: E731
+        entry = {"shape": list(w.shape), "io_dtype": w.dtype, "num_groups": w.groups}
+        for label, fn, nbytes in (("fwd", fwd, 2 * w.numel * eb), ("bwd", bwd, 3 * w.numel * eb)):
+            try:
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize(dev)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(10):
+                    fn()
+                b.record(stream)
+                torch.cuda.synchronize(dev)
+                ms = a.elapsed_time(b) / 10
+                entry[f"{label}_ms"] = ms
+                entry[f"{label}_frac"] = nbytes / (ms * 1e-3) / 1e9 / peak
+            except Exception as e:
+                entry[f"{label}_unavailable"] = f"{type(e).__name__}: {str(e)[:300]}"
+        if "fwd_ms" in entry and "bwd_ms" in entry:
+            entry["fwd_bwd_gelem_s"] = w.numel / ((entry["fwd_ms"] + entry["bwd_ms"]) * 1e-3) / 1e9
+        out[name] = entry
+        del x, gy, n, d
+        torch.cuda.empty_cache()
+    print(json.dumps(out), flush=True)
 
 
 def run_sweep(args):
@@ -1329,6 +1601,9 @@ def _bf16_peak():
 
 def main():
     args = parse_args()
+    if args.gpu_bar_child:
+        run_gpu_bar_child(args.gpu_bar_child.split(","))
+        return
     if args.workload == BSPLINE_WORKLOAD:
         if args.impl == "reference":
             run_bspline_reference(args)

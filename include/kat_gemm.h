@@ -79,6 +79,13 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h,
  * reset to 0.  Synchronous (reads a device word). */
 int kat_gemm_device_status(int device, int reset, int* status);
 
+/* Test only: on != 0 makes every following GEMM launch in this process stall its MMA issuer on
+ * a barrier that nothing completes, so the launch exercises its bounded-wait path (returns
+ * after about two seconds with KAT_DEVICE_WAIT_TIMEOUT in the status word and undefined
+ * outputs); on == 0 turns it off again.  Off by default; nothing but a test calls it.
+ * No counterpart in the reference, whose kernels have no device-side waits. */
+int kat_gemm_set_test_stall(int on);
+
 #ifdef __cplusplus
 }
 #endif

@@ -146,18 +146,21 @@ int kat_rational_fwd_f64(const double* x, double* y,
 
 /*
  * Backward without any device allocation, for callers that cannot allocate where they run
- * it: code inside a CUDA graph capture in the global capture mode (cudaMalloc is refused
- * there), plugin hosts whose operator interface provides input/output buffers but no
- * allocator, and fixed-budget real-time deployments where a mid-run cudaMalloc could stall
- * the device or fail.  Same arguments and results as kat_rational_bwd minus the workspace:
- * the partial sums go to a fixed 2 MiB file-scope device array instead, which every GPU
- * that loads this library holds until the process exits.
+ * it: plugin hosts whose operator interface hands the operator its input and output
+ * buffers but no allocator, and fixed-budget real-time loops where a cudaMalloc in the
+ * middle of a run could stall the device or fail.  Same arguments and results as
+ * kat_rational_bwd minus the workspace: the partial sums go to a fixed 2 MiB file-scope
+ * device array instead, which every GPU that loads this library holds until the process
+ * exits.
  *   - Problems whose backward needs more than 2 MiB of scratch
  *     (kat_rational_bwd_workspace_size) are rejected with KAT_ERR_SCRATCH_LIMIT before
  *     anything is enqueued.
  *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress, with that device current) and caches it; make that first call
- *     before any stream capture.  No call allocates (no cudaMalloc / cudaFree).
+ *     (cudaGetSymbolAddress, with that device current) and caches it for the life of the
+ *     process; make that first call before any stream capture.  The cached address belongs
+ *     to the device's current primary context: after cudaDeviceReset (or anything else that
+ *     destroys that context) do not call this entry point again in the same process.  No
+ *     call allocates (no cudaMalloc / cudaFree).
  *   - Every call on a device shares the one array and leaves the last call's partial sums in
  *     it; each call writes every entry it later reads, so nothing needs clearing.  Calls
  *     that can overlap on the GPU (different streams, or different host threads) race on
@@ -200,6 +203,9 @@ int kat_rational_device_status(int device, int reset, int* status);
  * k-th call of each rank pairs with the k-th call of the others.  A rank that does not
  * arrive within timeout_ms makes the others set KAT_DEVICE_EXCHANGE_TIMEOUT in the device
  * status word and write NaN gradients (the kernel returns; the context stays usable).
+ * Failure is fail-stop: a rank whose wait ran out marks its own exchange buffer broken, and
+ * every later call with that buffer writes NaN gradients and stores nothing to any peer, so
+ * no rank ever adds data of two different calls.  Rebuild the buffers (every rank) to go on.
  * Replaces the reference's (absent) distributed layer; no counterpart there.
  */
 #define KAT_MAX_PEERS 8

@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = (
     "kat_gemm_rational_bwd_workspace_bytes",
     "kat_gemm_rational_bwd",
     "kat_gemm_device_status",
+    "kat_gemm_set_test_stall",
 )
 
 KAT_MAX_PEERS = 8
@@ -145,6 +146,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_gemm_rational_bwd.restype = i32
     lib.kat_gemm_device_status.argtypes = [i32, i32, ctypes.POINTER(ctypes.c_int)]
     lib.kat_gemm_device_status.restype = i32
+    lib.kat_gemm_set_test_stall.argtypes = [i32]
+    lib.kat_gemm_set_test_stall.restype = i32
     lib.kat_bspline_basis_fwd.argtypes = [vp, vp, vp, i64, i64, ctypes.c_int32, ctypes.c_int32,
                                           vp]
     lib.kat_bspline_basis_fwd.restype = i32

@@ -47,6 +47,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "kat_rational.h"
@@ -467,7 +468,7 @@ kat_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   } else if (warp == 1) {
     // ---------------- MMA issuer (rank 0 of a pair issues for both CTAs) ----------------
     if (lane == 0 && rank == 0 && args.stall) {
-      // Test hook (KAT_GEMM_TEST_STALL=1): a wait that nothing completes runs out, sets the
+      // Test hook (kat_gemm_set_test_stall): a wait that nothing completes runs out, sets the
       // abort flag and the device status, and every role stops at its next wait.
       (void)wait_phase(drain, 0u, abort);
     } else if (lane == 0 && rank == 0) {
@@ -909,6 +910,10 @@ int pair_slots(int device) {
   return cache[device];
 }
 
+// Test hook, off unless kat_gemm_set_test_stall turned it on in this process: the next
+// launches' MMA issuer waits on a barrier nothing completes (the bounded-wait path).
+std::atomic<int> g_test_stall{0};
+
 template <int kMode, int kF, int kPair>
 int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int64_t k,
                 const CUtensorMap& o0, const CUtensorMap& o1, const CUtensorMap& h,
@@ -921,8 +926,7 @@ int launch_mode(const CUtensorMap& ma, const void* b, int64_t m, int64_t n, int6
   CUtensorMap mb;
   if (!make_map(&mb, b, n, k, kBK, uint32_t(kBN / kPair), CU_TENSOR_MAP_SWIZZLE_128B))
     return KAT_ERR_CUDA;
-  const char* stall = getenv("KAT_GEMM_TEST_STALL");
-  args.stall = (stall != nullptr && stall[0] == '1') ? 1 : 0;
+  args.stall = g_test_stall.load(std::memory_order_relaxed);
   args.m_tiles = int32_t((m + kBM * kPair - 1) / (kBM * kPair));
   args.num_tiles = int32_t(int64_t(args.m_tiles) * (n / kBN));
   const int sms = sm_count(device);
@@ -1107,6 +1111,11 @@ int kat_gemm_rational_bwd(const void* a, const void* b, const void* h, const flo
   kat_gemm_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, st>>>(
       static_cast<const double*>(workspace), grid, Cfg<kBwd>::kEpiWarps, num_groups, den, d_num, d_den, formula);
   return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
+}
+
+int kat_gemm_set_test_stall(int on) {
+  g_test_stall.store(on ? 1 : 0, std::memory_order_relaxed);
+  return KAT_OK;
 }
 
 int kat_gemm_device_status(int device, int reset, int* status) {

@@ -873,11 +873,22 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
 // The epoch is a per-buffer counter the kernel increments, so calls must be made the same
 // number of times on every rank (each rank's k-th call pairs with every other rank's k-th
 // call).  Two epoch halves let a rank run ahead by one call without overwriting data a
-// peer still reads.  A wait that runs out sets KAT_DEVICE_EXCHANGE_TIMEOUT in the device
-// status word and writes NaN gradients.
+// peer still reads: a rank can post call e + 1 only after it saw every flag reach e, and
+// call e + 2 only after every rank posted e + 1, which a rank does only once it has read
+// its call-e inbox.
+//
+// Failure is fail-stop.  A wait that runs out (or a flag seen more than one call ahead,
+// which the pairing above rules out unless some rank already gave up) sets
+// KAT_DEVICE_EXCHANGE_TIMEOUT in the device status word, writes NaN gradients and sets this
+// rank's `broken` word; every later call on a broken buffer writes NaN at once and stores
+// nothing to any peer.  A rank that gave up therefore never posts again, so a late peer can
+// only pair with data that was really posted for its call (it gets correct sums once, then
+// times out itself) and no rank ever adds data of two different calls.  Only local memory is
+// written after a failure: a peer that has gone away is never touched again.  The buffer
+// stays broken until it is rebuilt.
 //
 // Exchange buffer layout (every rank, zero-initialised once):
-//   [0]    u64 epoch                        [64]  u64 flags[kMaxPeers] (flag[src] = epoch)
+//   [0]    u64 epoch     [8] u64 broken     [64]  u64 flags[kMaxPeers] (flag[src] = epoch)
 //   [128]  f64 inbox[2][kMaxPeers][G][10]
 // ---------------------------------------------------------------------------
 
@@ -920,6 +931,8 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nwarps = blockDim.x >> 5;
+  char* const own = peers.buf[peers.rank];
+  uint64_t* const broken = reinterpret_cast<uint64_t*>(own + 8);
   // Programmatic dependent of the partial-sum kernel, as kat_bwd_reduce_kernel.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int g = warp; g < G; g += nwarps) {
@@ -930,52 +943,63 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
       if (lane == k) s_sum[g * kAcc + k] = tot[k];
   }
   if (tid == 0) {
-    uint64_t* ep = reinterpret_cast<uint64_t*>(peers.buf[peers.rank]);
+    uint64_t* ep = reinterpret_cast<uint64_t*>(own);
+    s_ok = *broken == 0 ? 1 : 0;
     s_epoch = *ep + 1;
-    *ep = s_epoch;
+    if (s_ok) *ep = s_epoch;
+    else atomicExch(&g_kat_status, kStatusExchangeTimeout);
   }
   __syncthreads();
   const uint64_t epoch = s_epoch;
   const size_t half = size_t(epoch & 1u) * kMaxPeers;
-  for (int r = 0; r < peers.world; ++r) {
-    double* dst = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader) +
-                  (half + size_t(peers.rank)) * size_t(n_out);
-    for (int i = tid; i < n_out; i += blockDim.x) dst[i] = s_sum[i];
+  if (s_ok) {
+    for (int r = 0; r < peers.world; ++r) {
+      double* dst = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader) +
+                    (half + size_t(peers.rank)) * size_t(n_out);
+      for (int i = tid; i < n_out; i += blockDim.x) dst[i] = s_sum[i];
+    }
   }
   __syncthreads();
-  if (tid == 0) {
+  if (tid == 0 && s_ok) {
     __threadfence_system();
     for (int r = 0; r < peers.world; ++r)
       st_release_sys(reinterpret_cast<uint64_t*>(peers.buf[r] + 64) + peers.rank, epoch);
-    const uint64_t* flags = reinterpret_cast<const uint64_t*>(peers.buf[peers.rank] + 64);
+    const uint64_t* flags = reinterpret_cast<const uint64_t*>(own + 64);
     const uint64_t limit = uint64_t(peers.timeout_ms) * 1000000ull;
     const uint64_t t0 = global_timer_ns();
     int ok = 1;
     for (int q = 0; q < peers.world && ok; ++q) {
-      while (ld_acquire_sys(flags + q) < epoch) {
+      uint64_t f;
+      while ((f = ld_acquire_sys(flags + q)) < epoch) {
         if (global_timer_ns() - t0 > limit) {
           ok = 0;
-          atomicExch(&g_kat_status, kStatusExchangeTimeout);
           break;
         }
         __nanosleep(64);
       }
+      if (ok && f > epoch + 1) ok = 0;   // out of step: some rank already gave up
+    }
+    if (!ok) {
+      *broken = 1;
+      atomicExch(&g_kat_status, kStatusExchangeTimeout);
     }
     s_ok = ok;
   }
   __syncthreads();
-  const double* inbox = reinterpret_cast<const double*>(peers.buf[peers.rank] + kExchangeHeader) +
+  const double* inbox = reinterpret_cast<const double*>(own + kExchangeHeader) +
                         half * size_t(n_out);
   const double scale = peers.average ? 1.0 / double(peers.world) : 1.0;
+  const bool ok = s_ok != 0;
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) {
       double v = 0.0;
-      for (int q = 0; q < peers.world; ++q) v += inbox[size_t(q) * n_out + g * kAcc + k];
+      if (ok)
+        for (int q = 0; q < peers.world; ++q) v += inbox[size_t(q) * n_out + g * kAcc + k];
       tot[k] = v;
     }
-    write_group(tot, scale, s_ok != 0, g, lane, den, dnum, dden, p.formula);
+    write_group(tot, scale, ok, g, lane, den, dnum, dden, p.formula);
   }
 }
 
@@ -2170,11 +2194,10 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
 // Backward without allocation.
 //
 // kat_rational_bwd needs a caller-allocated workspace for its per-block partial sums.  Some
-// callers cannot allocate device memory where they run the backward: code inside a CUDA
-// graph capture in the global capture mode (where cudaMalloc is refused), plugin hosts whose
+// callers cannot allocate device memory where they run the backward: plugin hosts whose
 // operator interface hands over input/output buffers but no allocator, and fixed-budget
-// real-time deployments where a mid-run cudaMalloc may stall the device or fail.  For them,
-// kat_rational_bwd_noalloc uses a fixed file-scope device array as that workspace.
+// real-time loops where a cudaMalloc in the middle of a run may stall the device or fail.
+// For them, kat_rational_bwd_noalloc uses a fixed file-scope device array as that workspace.
 // ---------------------------------------------------------------------------
 
 namespace {
@@ -2189,7 +2212,8 @@ std::mutex g_noalloc_mu;
 std::map<int, void*> g_noalloc_addr;
 
 // Device address of the scratch array on `dev`, which must be the current device; looked up
-// once per device and cached.
+// once per device and cached for the life of the process (the address of the device's
+// primary context at the first call: a cudaDeviceReset afterwards leaves it stale).
 cudaError_t noalloc_scratch_address(int dev, void** out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   auto it = g_noalloc_addr.find(dev);

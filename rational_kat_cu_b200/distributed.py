@@ -116,8 +116,9 @@ class PeerExchange:
     (all_gather_object); every rank maps the others' buffers on its own device with lazy
     peer access and checks each mapping with a small copy before any kernel uses it
     (kat_rational_exchange_open).  `peers` is the kat_rational_peers descriptor the
-    data-parallel backward takes.  Construction is collective; close() (also run at garbage
-    collection) unmaps and frees.
+    data-parallel backward takes.  Construction and close() are collective.  A failed
+    exchange (KAT_DEVICE_EXCHANGE_TIMEOUT) leaves the buffers broken: every later backward
+    through them writes NaN gradients until a new PeerExchange replaces this one.
     """
 
     def __init__(self, num_groups: int, group=None, average: bool = True,
@@ -132,6 +133,8 @@ class PeerExchange:
         self._lib = lib
         self._opened: List[int] = []
         self._local = None
+        self.group = group
+        self.device = device
         with torch.cuda.device(device):
             local = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
@@ -161,25 +164,40 @@ class PeerExchange:
         self.peers.timeout_ms = int(timeout_ms)
         for r, ptr in enumerate(ptrs):
             self.peers.buffers[r] = ctypes.c_void_p(ptr)
-        self.group = group
-        self.device = device
         dist.barrier(group=group)
 
     def close(self) -> None:
-        """Unmap the peers' buffers and free the local one (after all kernels using them)."""
+        """Collective teardown: every rank of the group must call it, after its last use.
+
+        Each rank waits for its own work on the device, unmaps the peers' buffers, then all
+        ranks meet at a barrier, and only then does each rank free its own buffer: a buffer is
+        never freed while another rank still maps it (freeing an exported allocation before
+        its importers close it is undefined).  If the barrier fails (a rank is gone), the
+        local buffer is left allocated and the error propagates."""
         if self._lib is None:
             return
-        torch.cuda.synchronize(self.device)
+        lib = self._lib
+        self._close_peers()
+        self._lib = None
+        dist.barrier(group=self.group)
+        if self._local is not None:
+            lib.kat_rational_exchange_destroy(ctypes.c_void_p(self._local))
+            self._local = None
+
+    def _close_peers(self) -> None:
+        if self.device is not None and self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         for ptr in self._opened:
             self._lib.kat_rational_exchange_close(ctypes.c_void_p(ptr))
         self._opened = []
-        if self._local is not None:
-            self._lib.kat_rational_exchange_destroy(ctypes.c_void_p(self._local))
-            self._local = None
-        self._lib = None
 
     def __del__(self):
+        # Garbage collection cannot run the collective part of close(): unmap the peers'
+        # buffers, but leave the local buffer allocated (it goes with the process) rather than
+        # free it under a peer that may still map it.
         try:
-            self.close()
+            if self._lib is not None:
+                self._close_peers()
+                self._lib = None
         except Exception:
             pass

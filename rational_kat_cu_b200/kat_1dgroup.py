@@ -85,5 +85,13 @@ class KAT_Group(nn.Module):
                                      timeout_ms=timeout_ms,
                                      device=self.weight_denominator.device)
 
+    def disable_data_parallel(self) -> None:
+        """Collective: release the exchange buffers enable_data_parallel set up (call it on
+        every rank, after the last backward through them) and return to the local backward."""
+        exchange = getattr(self, "exchange", None)
+        self.exchange = None
+        if exchange is not None:
+            exchange.close()
+
     def extra_repr(self) -> str:
         return f"num_groups={self.num_groups}, order={self.order}"

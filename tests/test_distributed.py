@@ -56,6 +56,46 @@ elif mode == "dead_peer":
     except Exception as e:
         print("RAISED", type(e).__name__)
     os._exit(0)
+elif mode.startswith("teardown"):
+    import json, time
+    from rational_kat_cu_b200.distributed import PeerExchange
+
+    class FakeLib:
+        """Records the exchange-buffer calls with a system-wide monotonic time stamp."""
+        def __init__(self):
+            self.log = []
+        def kat_rational_exchange_close(self, ptr):
+            self.log.append(("close", ptr.value, time.monotonic()))
+            return 0
+        def kat_rational_exchange_destroy(self, ptr):
+            self.log.append(("destroy", ptr.value, time.monotonic()))
+            return 0
+
+    pe = PeerExchange.__new__(PeerExchange)
+    pe._lib = FakeLib()
+    lib = pe._lib
+    pe._opened = [1000 + r for r in range(world) if r != rank]
+    pe._local = 2000 + rank
+    pe.group = None
+    pe.device = torch.device("cpu")
+    raised = None
+    if mode == "teardown":
+        if rank == 1:
+            time.sleep(1.0)        # a slow rank: the others must not free before it unmapped
+        pe.close()
+        pe.close()                 # idempotent
+    elif mode == "teardown_gc":
+        del pe
+    elif mode == "teardown_dead":
+        if rank == 1:
+            os._exit(0)
+        try:
+            pe.close()
+        except Exception as e:
+            raised = type(e).__name__
+    with open(f"{{out}}.{{rank}}.json", "w") as fh:
+        json.dump({{"log": lib.log, "raised": raised}}, fh)
+    os._exit(0)
 torch.save({{"num": m.weight_numerator.grad, "den": m.weight_denominator.grad}},
            f"{{out}}.{{rank}}.pt")
 dist.destroy_process_group()
@@ -85,6 +125,12 @@ def run_ranks(mode, world=2, timeout=120):
             path = f"{out}.{r}.pt"
             if os.path.exists(path):
                 results[r] = torch.load(path)
+            path = f"{out}.{r}.json"
+            if os.path.exists(path):
+                import json
+
+                with open(path) as fh:
+                    results[r] = json.load(fh)
         return outs, results
 
 
@@ -127,3 +173,29 @@ def test_shard_rows_partition(rows, world):
         sl = shard_rows(rows, r, world)
         seen.extend(range(rows)[sl])
     assert seen == list(range(rows))
+
+
+def test_peer_exchange_teardown_frees_only_after_every_rank_unmapped():
+    """close() is collective: each rank unmaps the peers' buffers, all meet at a barrier, and
+    only then does any rank free its own buffer, even when one rank is a second late."""
+    outs, res = run_ranks("teardown")
+    assert all(rc == 0 for rc, _, _ in outs), outs
+    closes = [t for r in res for op, _, t in res[r]["log"] if op == "close"]
+    destroys = [t for r in res for op, _, t in res[r]["log"] if op == "destroy"]
+    assert len(closes) == 2 and len(destroys) == 2       # one peer each; second close() no-op
+    assert min(destroys) > max(closes)
+    for r in res:
+        assert [e[1] for e in res[r]["log"] if e[0] == "destroy"] == [2000 + r]
+
+
+def test_peer_exchange_garbage_collection_unmaps_but_never_frees():
+    outs, res = run_ranks("teardown_gc")
+    assert all(rc == 0 for rc, _, _ in outs), outs
+    for r in res:
+        assert [e[0] for e in res[r]["log"]] == ["close"]
+
+
+def test_peer_exchange_teardown_with_a_dead_rank_raises_and_keeps_the_buffer():
+    outs, res = run_ranks("teardown_dead", timeout=90)
+    assert res[0]["raised"] is not None
+    assert [e[0] for e in res[0]["log"]] == ["close"]

@@ -346,13 +346,13 @@ from rational_kat_cu_b200 import fused_gemm as fg
 a = torch.randn(300, 128, device="cuda").to(torch.bfloat16)
 b = (torch.randn(512, 128, device="cuda") * 0.1).to(torch.bfloat16)
 assert fg.device_status(0, reset=True) == 0
-os.environ["KAT_GEMM_TEST_STALL"] = "1"
+_native.lib().kat_gemm_set_test_stall(1)
 t0 = time.time()
 fg.gemm_bf16(a, b)
 torch.cuda.synchronize()
 waited = time.time() - t0
 status = fg.device_status(0, reset=True)
-del os.environ["KAT_GEMM_TEST_STALL"]
+_native.lib().kat_gemm_set_test_stall(0)
 c = fg.gemm_bf16(a, b)
 torch.cuda.synchronize()
 err = float((c.double() - a.double() @ b.double().t()).abs().max())
@@ -361,7 +361,7 @@ print("result", status, round(waited, 2), err, fg.device_status(0))
 
 
 def test_stalled_pipeline_reports_and_recovers():
-    """A pipeline wait that nothing completes (test hook KAT_GEMM_TEST_STALL=1: the MMA issuer
+    """A pipeline wait that nothing completes (test hook kat_gemm_set_test_stall(1): the MMA issuer
     waits on a barrier no one arrives at) runs out after its clock limit: the kernel returns,
     the sticky status reads KAT_DEVICE_WAIT_TIMEOUT, tensor memory is freed, and the next
     launch in the same context computes correctly."""
@@ -371,7 +371,6 @@ def test_stalled_pipeline_reports_and_recovers():
 
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     env = dict(os.environ)
-    env.pop("KAT_GEMM_TEST_STALL", None)
     res = subprocess.run([sys.executable, "-c", STALL_CHILD.format(repo=repo)], env=env,
                          capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
