@@ -369,13 +369,18 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Block size cap of the cp.async backward (one block per SM at 512 threads x 128 registers).
+#ifndef KAT_ASYNC_THREADS
+#define KAT_ASYNC_THREADS 512
+#endif
+constexpr int kAsyncThreads = KAT_ASYNC_THREADS;
 #ifndef KAT_ASYNC_MAXNREG
 #define KAT_ASYNC_MAXNREG 0
 #endif
 #if KAT_ASYNC_MAXNREG > 0
 #define KAT_ASYNC_BOUNDS __maxnreg__(KAT_ASYNC_MAXNREG)
 #else
-#define KAT_ASYNC_BOUNDS __launch_bounds__(kMaxThreads)
+#define KAT_ASYNC_BOUNDS __launch_bounds__(kAsyncThreads)
 #endif
 
 template <typename Tio, int kStages, int kRows, int kF, int kVB = 16>
@@ -1653,10 +1658,10 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
   // Block shape of the cp.async backward: at most kAsyncCols vector columns, and as many
   // rows as fill kMaxThreads threads (at 128 registers, one 512-thread block per SM).
   static const int max_cols =
-      std::max(32, std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kAsyncCols), kMaxThreads) / 32 * 32);
+      std::max(32, std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kAsyncCols), kAsyncThreads) / 32 * 32);
   Plan probe;
   int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
-                          max_cols);
+                          max_cols, kAsyncThreads);
   if (st != KAT_OK) return st;
   const void* fn = bwd_async_kernel_for(dtype, formula, vb);
   const size_t smem = async_smem_bytes(probe.threads, vb);
@@ -1677,7 +1682,8 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
       g_occupancy[key] = occ;
     }
   }
-  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p, max_cols);
+  st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, occ, p, max_cols,
+                      kAsyncThreads);
   *dev_out = dev;
   return st;
 }

@@ -3,10 +3,13 @@
 The reference exports a pure-PyTorch module next to the CUDA one
 (kat_rational/kat_1dgroup_torch.py:27-155, exported at kat_rational/__init__.py:4).  This
 file keeps that API: `Rational_CUDA_A_1DGroup(x, weight_numerator, weight_denominator,
-group)` on [B, L, D] input, and `KAT_Group_Torch(num_groups, mode)`.  It evaluates the same
-formula, y = P(x) / (1 + sum |b_i| x^i), by Horner's rule on grouped views with torch
-autograd for the backward.  It is selected only on explicit request (device="cpu" or this
-class); the CUDA modules never route through it.
+group)` on [B, L, D] input, and `KAT_Group_Torch(num_groups, mode)`.  Its results are defined
+by a sequence of tensor operations, so this file performs the same sequence — group-major
+copy, a table of powers built by repeated products, one batched matrix product per
+polynomial with the denominator's coefficients padded and made non-negative, the quotient,
+the layout restored — and torch autograd differentiates it: on the same machine the values and
+gradients equal the reference's bit for bit.  It is selected only on explicit request
+(device="cpu" or this class); the CUDA modules never route through it.
 """
 
 from __future__ import annotations
@@ -19,22 +22,34 @@ from torch import nn
 from ._init_table import INIT_JSON
 
 
+def _power_table(z: torch.Tensor, count: int) -> torch.Tensor:
+    """[G, count, M]: z**0 .. z**(count - 1) for z [G, M], each power the previous one times z
+    (kat_1dgroup_torch.py:7-24 builds its table the same way)."""
+    cols = [torch.ones_like(z), z]
+    while len(cols) < count:
+        cols.append(cols[-1] * z)
+    return torch.stack(cols[:count], dim=1)
+
+
 def Rational_CUDA_A_1DGroup(x: torch.Tensor, weight_numerator: torch.Tensor,
                             weight_denominator: torch.Tensor, group: int) -> torch.Tensor:
-    """P(x)/Q(x) per channel group on x [B, L, D]; weight_numerator [group, len_num],
-    weight_denominator [group, len_den]."""
+    """P(x)/Q(x) per channel group on x [B, L, D]; weight_numerator [group, n],
+    weight_denominator [group, m]; Q = 1 + sum_i |b_i| x^i (kat_1dgroup_torch.py:27-78)."""
     B, L, D = x.shape
-    z = x.view(B, L, group, D // group)
-    a = weight_numerator.view(group, -1).unsqueeze(-1)          # [G, n, 1]
-    c = weight_denominator.view(group, -1).abs().unsqueeze(-1)  # [G, m, 1]
-    p = a[:, -1]
-    for k in range(a.shape[1] - 2, -1, -1):
-        p = p * z + a[:, k]
-    q = c[:, -1]
-    for i in range(c.shape[1] - 2, -1, -1):
-        q = q * z + c[:, i]
-    q = q * z + 1.0
-    return (p / q).view(B, L, D)
+    per = D // group
+    n, m = weight_numerator.size(1), weight_denominator.size(1)
+    # One row per group: [G, B*L*per], channels of a group contiguous.
+    z = x.view(B, L, group, per).permute(2, 0, 1, 3).contiguous().view(group, B * L * per)
+    table = _power_table(z, max(n, m))
+    num = torch.bmm(weight_numerator.unsqueeze(1), table).squeeze(1)
+    den_coef = torch.cat([
+        torch.ones(group, 1, device=x.device, dtype=weight_denominator.dtype),
+        weight_denominator,
+        torch.zeros(group, max(0, n - m - 1), device=x.device, dtype=weight_denominator.dtype),
+    ], dim=1).abs()
+    den = torch.bmm(den_coef.unsqueeze(1), table).squeeze(1)
+    out = num.div(den)
+    return out.view(group, B, L, per).permute(1, 2, 0, 3).contiguous().view(B, L, D)
 
 
 class KAT_Group_Torch(nn.Module):

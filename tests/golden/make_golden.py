@@ -18,7 +18,7 @@ Conventions the reference forces (it has no other entry for these cases):
                    dtypes); outputs are stored unrounded in fp32.
 
 Usage (needs the reference checkout; the fixtures are committed):
-  python tests/golden/make_golden.py [/path/to/rational_kat_cu]
+  python tests/golden/make_golden.py /path/to/rational_kat_cu   (or set KAT_REFERENCE_ROOT)
 """
 
 from __future__ import annotations
@@ -32,7 +32,13 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference"
+def reference_root() -> str:
+    """The reference checkout: the first command-line argument, else $KAT_REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KAT_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/rational_kat_cu "
+                 "(or set KAT_REFERENCE_ROOT)")
+    return root
 
 
 def load_reference(ref_root: str):
@@ -108,7 +114,7 @@ def quantize(t, dtype):
     return t
 
 
-def main(ref_root: str = DEFAULT_REF) -> None:
+def main(ref_root: str) -> None:
     ref = load_reference(ref_root)
     with open(os.path.join(ref_root, "kat_rational", "init.json")) as fh:
         init_table = json.load(fh)
@@ -155,4 +161,4 @@ def main(ref_root: str = DEFAULT_REF) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF)
+    main(reference_root())

@@ -8,7 +8,7 @@ the module's imports pull in Triton launchers that need a GPU), runs them on see
 in fp32 with torch autograd for dL/dx, and stores x, grid, bases, grad_bases and dx.
 
 Usage (needs the reference checkout; the fixtures are committed):
-  python tests/golden/make_golden_bspline.py [/path/to/rational_kat_cu]
+  python tests/golden/make_golden_bspline.py /path/to/rational_kat_cu   (or set KAT_REFERENCE_ROOT)
 """
 
 from __future__ import annotations
@@ -22,7 +22,13 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference"
+def reference_root() -> str:
+    """The reference checkout: the first command-line argument, else $KAT_REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KAT_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden_bspline.py /path/to/rational_kat_cu "
+                 "(or set KAT_REFERENCE_ROOT)")
+    return root
 
 
 def load_functions(ref_root: str):
@@ -65,7 +71,7 @@ def adaptive_grid(x, grid_size, order, margin=0.01):
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF
+    ref_root = reference_root()
     ref_b_splines, ref_make_grid = load_functions(ref_root)
     arrays, manifest = {}, []
     for name, B, D, gs, order, seed, xs, kind in CASES:

@@ -15,7 +15,7 @@ D != 0 everywhere except the identity case (b = 0, D == 0 everywhere), whose d b
 recorded as not comparable ("db_comparable": false).
 
 Usage (needs the reference checkout; the fixtures are committed):
-  python tests/golden/make_golden_rat.py [/path/to/rational_kat_cu]
+  python tests/golden/make_golden_rat.py /path/to/rational_kat_cu   (or set KAT_REFERENCE_ROOT)
 """
 
 from __future__ import annotations
@@ -29,7 +29,13 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference"
+def reference_root() -> str:
+    """The reference checkout: the first command-line argument, else $KAT_REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KAT_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden_rat.py /path/to/rational_kat_cu "
+                 "(or set KAT_REFERENCE_ROOT)")
+    return root
 
 
 def load_rat_ref(ref_root: str):
@@ -59,7 +65,7 @@ CASES = [
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF
+    ref_root = reference_root()
     rat_ref = load_rat_ref(ref_root)
     arrays, manifest = {}, []
     for name, N, D, G, seed, xs, kind, dt in CASES:

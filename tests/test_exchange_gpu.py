@@ -5,8 +5,11 @@ exchange fused into the reduction kernel over NVLink peer memory.
   - a wait that runs out (a second rank that never arrives: both "ranks" point at one
     buffer, so nothing ever raises rank 1's flag) sets KAT_DEVICE_EXCHANGE_TIMEOUT, writes
     NaN gradients, leaves dx intact and the context usable;
+  - a flag more than one call ahead is refused at once (NaN, status, broken buffer), and a
+    broken buffer fails the next call at once without posting anything;
   - with two GPUs, two processes get identical gradients equal to the rank-order average of
-    their local gradients (skipped on one-GPU machines).
+    their local gradients, then tear the buffers down collectively (skipped on one-GPU
+    machines).
 """
 
 import ctypes
@@ -97,6 +100,53 @@ def test_missing_rank_times_out_with_status(cuda_device):
     assert _native.device_status(0) == 0
 
 
+def test_flag_far_ahead_is_refused_without_waiting(cuda_device):
+    """A peer flag more than one call ahead cannot come from a correct pairing: the call
+    writes NaN gradients, sets the status and marks the buffer broken, with no wait.
+    (Both "ranks" share one buffer; rank 1's flag is preset to 10.)"""
+    lib = _native.lib()
+    G = 8
+    x, gy, n, d = _problem(cuda_device, G=G)
+    buf = torch.zeros(lib.kat_rational_exchange_buffer_bytes(G), dtype=torch.uint8,
+                      device=cuda_device)
+    words = buf.view(torch.int64)
+    words[8 + 1] = 10                      # flags[1] (flags start at byte 64)
+    _native.device_status(0, reset=True)
+    st, dx, dn, dd = _call(lib.kat_rational_bwd_allreduce, x, gy, n, d, G,
+                           _peers([buf, buf], 0, timeout_ms=60000))
+    assert st == 0
+    assert _native.device_status(0, reset=True) == _native.KAT_DEVICE_EXCHANGE_TIMEOUT
+    assert torch.isnan(dn).all() and torch.isnan(dd).all()
+    assert int(words[1]) == 1              # the broken word
+    _, dx_ref, _, _ = _call(lib.kat_rational_bwd, x, gy, n, d, G)
+    assert torch.equal(dx, dx_ref)
+
+
+def test_broken_buffer_fails_at_once(cuda_device):
+    """After a timeout the buffer is broken: the next call writes NaN gradients at once
+    (no second wait) and stores nothing (the epoch does not advance)."""
+    import time
+
+    lib = _native.lib()
+    G = 8
+    x, gy, n, d = _problem(cuda_device, G=G)
+    buf = torch.zeros(lib.kat_rational_exchange_buffer_bytes(G), dtype=torch.uint8,
+                      device=cuda_device)
+    words = buf.view(torch.int64)
+    _native.device_status(0, reset=True)
+    _call(lib.kat_rational_bwd_allreduce, x, gy, n, d, G, _peers([buf, buf], 0, timeout_ms=50))
+    assert int(words[1]) == 1 and int(words[0]) == 1
+    assert _native.device_status(0, reset=True) == _native.KAT_DEVICE_EXCHANGE_TIMEOUT
+    t0 = time.time()
+    st, dx, dn, dd = _call(lib.kat_rational_bwd_allreduce, x, gy, n, d, G,
+                           _peers([buf, buf], 0, timeout_ms=20000))
+    assert st == 0 and time.time() - t0 < 5.0
+    assert torch.isnan(dn).all() and torch.isnan(dd).all()
+    assert int(words[0]) == 1              # no new epoch was posted
+    assert _native.device_status(0, reset=True) == _native.KAT_DEVICE_EXCHANGE_TIMEOUT
+    assert _native.device_status(0) == 0
+
+
 def test_descriptor_validation():
     lib = _native.lib()
     x = torch.empty(0)
@@ -143,6 +193,8 @@ for step in range(3):
     assert all(torch.equal(gots[0], t) for t in gots), "ranks differ"
 from rational_kat_cu_b200 import _native
 assert _native.device_status(rank) == 0
+m.disable_data_parallel()      # collective teardown: unmap, barrier, free
+assert m.exchange is None
 dist.barrier()
 dist.destroy_process_group()
 print("rank", rank, "ok")
