@@ -190,6 +190,10 @@ int kat_rational_bwd_workspace_size(int64_t batch, int64_t channels, int64_t inn
  * No counterpart in the reference, whose kernels have no device-side waits.
  */
 #define KAT_DEVICE_WAIT_TIMEOUT 1
+/* Set only by the bounds-checked debug build of this library (libkat_rational_debug.so,
+ * compiled with -DKAT_DEBUG_BOUNDS=1): a kernel found a global access, a workspace slot or a
+ * plan invariant out of range and skipped the access instead of making it. */
+#define KAT_DEVICE_BOUNDS 3
 int kat_rational_device_status(int device, int reset, int* status);
 
 /*

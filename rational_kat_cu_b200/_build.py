@@ -3,7 +3,10 @@
 `build()` runs nvcc on csrc/kat_rational.cu, csrc/kat_bspline.cu and csrc/kat_gemm.cu for
 `-gencode arch=compute_100a,code=sm_100a` and writes the shared library next to this file, so
 it travels with the source tree.  It rebuilds only when a source or a public header is newer
-than the library.
+than the library.  `build(debug=True)` writes libkat_rational_debug.so from the same sources
+with -DKAT_DEBUG_BOUNDS=1: every global access, workspace slot and plan invariant of the
+activation kernels is checked, and a violation sets KAT_DEVICE_BOUNDS in the device status
+word instead of being made (the GPU-side stand-in for compute-sanitizer; tests only).
 """
 
 from __future__ import annotations
@@ -21,8 +24,10 @@ SOURCES = [os.path.join(PKG_DIR, "csrc", "kat_rational.cu"),
 HEADERS = [os.path.join(REPO_DIR, "include", "kat_rational.h"),
            os.path.join(REPO_DIR, "include", "kat_bspline.h"),
            os.path.join(REPO_DIR, "include", "kat_gemm.h"),
-           os.path.join(PKG_DIR, "csrc", "kat_math.cuh")]
+           os.path.join(PKG_DIR, "csrc", "kat_math.cuh"),
+           os.path.join(PKG_DIR, "csrc", "kat_plan.h")]
 LIBRARY = os.path.join(PKG_DIR, "libkat_rational.so")
+DEBUG_LIBRARY = os.path.join(PKG_DIR, "libkat_rational_debug.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -40,19 +45,20 @@ def find_nvcc() -> str:
     raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
 
 
-def is_stale() -> bool:
-    if not os.path.exists(LIBRARY):
+def is_stale(target: str = LIBRARY) -> bool:
+    if not os.path.exists(target):
         return True
-    lib_t = os.path.getmtime(LIBRARY)
+    lib_t = os.path.getmtime(target)
     return any(os.path.getmtime(p) > lib_t for p in (*SOURCES, *HEADERS, __file__))
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile the library if needed; return its path."""
-    if not force and not is_stale():
-        return LIBRARY
+def build(force: bool = False, verbose: bool = False, debug: bool = False) -> str:
+    """Compile the library (or its bounds-checked debug build) if needed; return its path."""
+    target = DEBUG_LIBRARY if debug else LIBRARY
+    if not force and not is_stale(target):
+        return target
     cmd = [find_nvcc(), *NVCC_FLAGS, "-I", os.path.join(REPO_DIR, "include"),
-           "-o", LIBRARY + ".tmp", *SOURCES]
+           *(["-DKAT_DEBUG_BOUNDS=1"] if debug else []), "-o", target + ".tmp", *SOURCES]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
@@ -61,9 +67,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose:
         print(res.stderr, file=sys.stderr)
-    os.replace(LIBRARY + ".tmp", LIBRARY)
-    return LIBRARY
+    os.replace(target + ".tmp", target)
+    return target
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv,
+                debug="--debug" in sys.argv))

@@ -52,50 +52,45 @@ namespace {
 
 #include "kat_math.cuh"
 
-constexpr int kMaxThreads = 512;  // block size cap
+#include "kat_plan.h"
+
+static_assert(kPlanSums == kAcc, "workspace slots per group: the 10 gradient moments");
 constexpr int kReduceThreads = kAcc * 32;
-constexpr int64_t kMaxElements = int64_t(1) << 48;
-constexpr int64_t kMaxBlocks = int64_t(1) << 14;
 
-// Launch geometry shared by host and device (a POD copy of kat_rational_plan).
-struct Plan {
-  int64_t rows;
-  int64_t width;
-  int64_t group_width;
-  int64_t num_groups;
-  int64_t vec_cols;    // vectors per row
-  int64_t vec_group;   // vectors per group
-  int64_t col_blocks;
-  int64_t items;
-  int64_t blocks;
-  int32_t vec;
-  int32_t threads;
-  int32_t tile_cols;
-  int32_t tile_rows;
-  int32_t max_segments;
-  int32_t max_local_groups;
-  uint64_t workspace_bytes;
-  int64_t items_q;     // items per block, floor(items / blocks)
-  int64_t items_r;     // the first items_r blocks take one more item
-  uint64_t rows_m;     // multiply-shift constants for dividing by rows ...
-  uint64_t vg_m;       // ... and by vec_group
-  int32_t rows_s1, rows_s2, vg_s1, vg_s2;
-  int32_t formula;     // KAT_FORMULA_*: how the reduction signs the denominator terms
-};
+__device__ int g_kat_status;  // sticky device status (0 = ok), read by kat_rational_device_status
 
-// Division by an invariant divisor d >= 1 with a multiply and shifts (Granlund and
-// Montgomery, "Division by invariant integers using multiplication", PLDI 1994, the
-// round-up method of their Figure 4.1 for N = 64): with l = ceil(log2 d),
-// m = floor(2^64 (2^l - d) / d) + 1, sh1 = min(l, 1), sh2 = max(l - 1, 0):
-//   t = mulhi(m, n);  n / d = (t + ((n - t) >> sh1)) >> sh2   for all 0 <= n < 2^64.
-void make_divider(uint64_t d, uint64_t* m, int32_t* s1, int32_t* s2) {
-  int l = 0;
-  while (l < 64 && (uint64_t(1) << l) < d) ++l;
-  const unsigned __int128 two64 = (unsigned __int128)1 << 64;
-  const unsigned __int128 num = two64 * (((unsigned __int128)1 << l) - d);
-  *m = uint64_t(num / d + 1);
-  *s1 = l < 1 ? l : 1;
-  *s2 = l - 1 > 0 ? l - 1 : 0;
+// Bounds-checked build (-DKAT_DEBUG_BOUNDS=1: libkat_rational_debug.so).  Every global access
+// of the activation kernels, every workspace slot and the plan's segment / group invariants
+// are checked before the access is made: a violation sets KAT_DEVICE_BOUNDS in the sticky
+// status word and the access is skipped — never a trap, so a shared GPU is never faulted.
+// In the release build the checks compile away.
+constexpr int kStatusBounds = KAT_DEVICE_BOUNDS;
+#ifndef KAT_DEBUG_BOUNDS
+#define KAT_DEBUG_BOUNDS 0
+#endif
+__device__ __forceinline__ bool kat_check(bool ok) {
+#if KAT_DEBUG_BOUNDS
+  if (!ok) atomicExch(&g_kat_status, kStatusBounds);
+  return ok;
+#else
+  (void)ok;
+  return true;
+#endif
+}
+// [ptr, ptr + n) inside [base, base + count) (element units).
+template <typename T>
+__device__ __forceinline__ bool in_bounds(const T* base, int64_t count, const T* ptr,
+                                          int64_t n = 1) {
+#if KAT_DEBUG_BOUNDS
+  const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+  const uintptr_t q = reinterpret_cast<uintptr_t>(ptr);
+  const bool ok = q >= b && (q - b) % sizeof(T) == 0 && n >= 0 &&
+                  int64_t((q - b) / sizeof(T)) <= count - n;
+  return kat_check(ok);
+#else
+  (void)base; (void)count; (void)ptr; (void)n;
+  return true;
+#endif
 }
 
 __device__ __forceinline__ int64_t fast_div(int64_t n, uint64_t m, int32_t s1, int32_t s2) {
@@ -141,6 +136,9 @@ __device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float*
   const int64_t g_last = (col_end - 1) / p.vec_group;
   const int n_out = int(g_last - g_first + 1) * kAcc;
   const int64_t span = min(int64_t(p.tile_cols), p.vec_group) * p.tile_rows;
+  const int64_t ws_count = int64_t(p.workspace_bytes / sizeof(double));
+  kat_check(seg >= 0 && seg < p.max_segments && g_last - g_first < p.max_local_groups &&
+            stride >= p.tile_rows * p.tile_cols && nthreads <= stride);
   if (span > 32) {
     // Wide groups: warp w adds outputs w, w + nwarps, ...; lane j takes columns j, j+32, ...
     // of every row, then a fixed xor tree.
@@ -161,7 +159,8 @@ __device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float*
       }
 #pragma unroll
       for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-      if (lane == 0) partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+      double* dst = partial + ((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k;
+      if (lane == 0 && in_bounds(partial, ws_count, dst)) *dst = v;
     }
   } else {
     // Narrow groups: thread o adds output o = (local group, slot) over its rows and columns.
@@ -177,7 +176,8 @@ __device__ __forceinline__ void segment_reduce(const float (&sums)[kAcc], float*
         const float* row = base + r * p.tile_cols;
         for (int c = tlo; c < thi; ++c) v += double(row[c]);
       }
-      partial[((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k] = v;
+      double* dst = partial + ((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc + k;
+      if (in_bounds(partial, ws_count, dst)) *dst = v;
     }
   }
   participants_sync<kNamed>(nthreads);
@@ -217,20 +217,22 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
       const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
       const Tio* xp = x + r0 * p.width + col * V;
       Tio* yp = y + r0 * p.width + col * V;
+      const int64_t n_elems = p.rows * p.width;
       Raw cur[U];
 #pragma unroll
       for (int u = 0; u < U; ++u)
-        if (u < n) cur[u] = load_raw<Tio, V>(xp + u * step);
+        if (u < n && in_bounds(x, n_elems, xp + u * step, V)) cur[u] = load_raw<Tio, V>(xp + u * step);
       xp += U * step;
 #pragma unroll 1
       for (int64_t b = 0; b < n; b += U) {
         Raw nxt[U];
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (b + U + u < n) nxt[u] = load_raw<Tio, V>(xp + u * step);
+          if (b + U + u < n && in_bounds(x, n_elems, xp + u * step, V))
+            nxt[u] = load_raw<Tio, V>(xp + u * step);
 #pragma unroll
         for (int u = 0; u < U; ++u)
-          if (b + u < n)
+          if (b + u < n && in_bounds(y, n_elems, yp + u * step, V))
             store_raw<Tio, V>(yp + u * step, fwd_vec<Tio, V, L, kExact, kF>(cur[u], c));
 #pragma unroll
         for (int u = 0; u < U; ++u) cur[u] = nxt[u];
@@ -284,10 +286,12 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
       const Tio* xp = x + off;
       const Tio* gp = gy + off;
       Tio* dp = write_dx ? dx + off : nullptr;
+      const int64_t n_elems = p.rows * p.width;
       Raw cx[U], cg[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (u < n) {
+        if (u < n && in_bounds(x, n_elems, xp + u * step, V) &&
+            in_bounds(gy, n_elems, gp + u * step, V)) {
           cx[u] = load_raw<Tio, V>(xp + u * step);
           cg[u] = load_raw<Tio, V>(gp + u * step);
         }
@@ -299,7 +303,8 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
         Raw nx[U], ng[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          if (b + U + u < n) {
+          if (b + U + u < n && in_bounds(x, n_elems, xp + u * step, V) &&
+              in_bounds(gy, n_elems, gp + u * step, V)) {
             nx[u] = load_raw<Tio, V>(xp + u * step);
             ng[u] = load_raw<Tio, V>(gp + u * step);
           }
@@ -308,7 +313,8 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
         for (int u = 0; u < U; ++u) {
           if (b + u < n) {
             const Raw d = bwd_vec<Tio, V, L, kRefine, kF>(cx[u], cg[u], c, acc);
-            if (write_dx) store_raw<Tio, V>(dp + u * step, d);
+            if (write_dx && in_bounds(dx, n_elems, dp + u * step, V))
+              store_raw<Tio, V>(dp + u * step, d);
           }
         }
 #pragma unroll
@@ -429,6 +435,7 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
       const Tio* lx = x + off;   // next rows to load
       const Tio* lg = gy + off;
       Tio* dp = write_dx ? dx + off : nullptr;
+      const int64_t n_elems = p.rows * p.width;
       int load_stage = 0;
       int load_row = 0;
       // Issue the loads of the next batch (rows load_row .. load_row + kRows - 1).
@@ -437,8 +444,10 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
 #pragma unroll
         for (int u = 0; u < kRows; ++u) {
           if (load_row + u < n) {
-            cp_async_vec<kVB>(sp + u * slot_stride, lx);
-            cp_async_vec<kVB>(sp + u * slot_stride + T, lg);
+            if (in_bounds(x, n_elems, lx, V) && in_bounds(gy, n_elems, lg, V)) {
+              cp_async_vec<kVB>(sp + u * slot_stride, lx);
+              cp_async_vec<kVB>(sp + u * slot_stride + T, lg);
+            }
             lx += step;
             lg += step;
           }
@@ -462,7 +471,7 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
             const Slot rg = sp[u * slot_stride + T];
             const Slot d = bwd_vec<Tio, V, L, kRefine, kF>(rx, rg, c, acc);
             if (write_dx) {
-              store_raw<Tio, V>(dp, d);
+              if (in_bounds(dx, n_elems, dp, V)) store_raw<Tio, V>(dp, d);
               dp += step;
             }
           }
@@ -500,6 +509,9 @@ __device__ __forceinline__ void group_totals(const double* __restrict__ partial,
       if (g > g_last) continue;
       const double* src =
           partial + ((blk * p.max_segments + (cb - cb0)) * p.max_local_groups + (g - g_first)) * kAcc;
+      if (!kat_check(cb - cb0 < p.max_segments && g - g_first < p.max_local_groups) ||
+          !in_bounds(partial, int64_t(p.workspace_bytes / sizeof(double)), src, kAcc))
+        continue;
 #pragma unroll
       for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
     }
@@ -580,8 +592,6 @@ struct Pipe {
 constexpr int kStatusWaitTimeout = 1;
 constexpr long long kWaitCycles = 4000000000LL;
 constexpr uint32_t kPipeHeader = 256;  // barriers + abort flag, keeps slots 128-byte aligned
-
-__device__ int g_kat_status;  // sticky device status (0 = ok), read by kat_rational_device_status
 
 __device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
@@ -700,6 +710,20 @@ __device__ __forceinline__ void produce(const Tio* __restrict__ in0, const Tio* 
     if (k >= uint32_t(q.stages) && !mbar_wait(&empty[s], ((k / q.stages) - 1) & 1u, abort)) break;
     const int64_t col0 = cb * p.tile_cols;
     const uint32_t row_bytes = uint32_t(min(int64_t(p.tile_cols), p.vec_cols - col0)) * 16u;
+    {
+      // The tile's first and last element of every tensor, and its slot, in range.
+      const int64_t n_elems = p.rows * p.width;
+      const int64_t first = row * p.width + col0 * V;
+      const int64_t last_end = (row + nrows - 1) * p.width + col0 * V + row_bytes / sizeof(Tio);
+      const bool ok = in_bounds(in0, n_elems, in0 + first, last_end - first) &&
+                      (kTensors == 1 || in_bounds(in1, n_elems, in1 + first, last_end - first)) &&
+                      kat_check(uint32_t(nrows) <= uint32_t(q.stage_rows) &&
+                                row_bytes <= uint32_t(q.seg_bytes));
+      if (!ok) {
+        *abort = 1;
+        break;
+      }
+    }
     mbar_arrive_expect_tx(&full[s], row_bytes * uint32_t(nrows) * kTensors);
 #pragma unroll
     for (int t = 0; t < kTensors; ++t) {
@@ -780,7 +804,8 @@ kat_fwd_tma_kernel(const Tio* __restrict__ x, Tio* __restrict__ y, const float* 
       Tio* dst = y + row * p.width + col * V;
       for (int j = tr; j < nrows; j += p.tile_rows) {
         const Raw raw = *reinterpret_cast<const Raw*>(src + size_t(j) * q.seg_bytes);
-        store_raw<Tio, V>(dst + int64_t(j) * p.width, fwd_vec<Tio, V, float2, kExact>(raw, c));
+        if (in_bounds(y, p.rows * p.width, dst + int64_t(j) * p.width, V))
+          store_raw<Tio, V>(dst + int64_t(j) * p.width, fwd_vec<Tio, V, float2, kExact>(raw, c));
       }
     }
     __syncwarp();
@@ -846,7 +871,8 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
         const Raw rx = *reinterpret_cast<const Raw*>(xs + size_t(j) * q.seg_bytes);
         const Raw rg = *reinterpret_cast<const Raw*>(gs + size_t(j) * q.seg_bytes);
         const Raw d = bwd_vec<Tio, V, float2, kRefine>(rx, rg, c, acc);
-        if (write_dx) store_raw<Tio, V>(dst + int64_t(j) * p.width, d);
+        if (write_dx && in_bounds(dx, p.rows * p.width, dst + int64_t(j) * p.width, V))
+          store_raw<Tio, V>(dst + int64_t(j) * p.width, d);
       }
     }
     __syncwarp();
@@ -959,8 +985,9 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   const size_t half = size_t(epoch & 1u) * kMaxPeers;
   if (s_ok) {
     for (int r = 0; r < peers.world; ++r) {
-      double* dst = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader) +
-                    (half + size_t(peers.rank)) * size_t(n_out);
+      double* inbox = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader);
+      double* dst = inbox + (half + size_t(peers.rank)) * size_t(n_out);
+      if (!in_bounds(inbox, int64_t(2) * kMaxPeers * n_out, dst, n_out)) continue;
       for (int i = tid; i < n_out; i += blockDim.x) dst[i] = s_sum[i];
     }
   }
@@ -1021,7 +1048,6 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
 constexpr int kUnroll = KAT_FWD_UNROLL;
 constexpr int kUnrollBwd = KAT_BWD_UNROLL;
 
-int elem_bytes(int dtype) { return dtype == KAT_DTYPE_F32 ? 4 : 2; }
 
 // Programmatic dependent launch: the forward, the cp.async backward and the grid reductions are
 // launched with programmatic stream serialization, so each can be launched while the previous
@@ -1049,87 +1075,6 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
-}
-
-int validate_dims(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-                  int64_t* n_elems) {
-  if (dtype != KAT_DTYPE_F32 && dtype != KAT_DTYPE_F16 && dtype != KAT_DTYPE_BF16)
-    return KAT_ERR_BAD_DTYPE;
-  if (batch < 0 || channels < 0 || inner < 0) return KAT_ERR_BAD_SHAPE;
-  if (num_groups < 1 || channels % num_groups != 0) return KAT_ERR_BAD_GROUPS;
-  if (inner != 0 && channels > kMaxElements / inner) return KAT_ERR_BAD_SHAPE;
-  const int64_t width = channels * inner;
-  if (width != 0 && batch > kMaxElements / width) return KAT_ERR_BAD_SHAPE;
-  *n_elems = batch * width;
-  return KAT_OK;
-}
-
-int max_vec_for(int dtype) { return 16 / elem_bytes(dtype); }
-
-int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_groups, int dtype,
-                   int vec, int sm_count, int ctas_per_sm, Plan* p, int max_cols = kMaxThreads,
-                   int max_threads = kMaxThreads) {
-  int64_t n = 0;
-  int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
-  if (st != KAT_OK) return st;
-  if (sm_count < 1 || ctas_per_sm < 1) return KAT_ERR_BAD_SHAPE;
-  memset(p, 0, sizeof(*p));
-  p->rows = batch;
-  p->width = channels * inner;
-  p->group_width = (channels / num_groups) * inner;
-  p->num_groups = num_groups;
-  const int vmax = max_vec_for(dtype);
-  if (vec == 0) {
-    vec = vmax;
-    while (vec > 1 && p->group_width % vec != 0) vec >>= 1;
-  } else if (vec < 1 || vec > vmax || (vec & (vec - 1)) != 0 || p->group_width % vec != 0) {
-    return KAT_ERR_BAD_SHAPE;
-  }
-  p->vec = vec;
-  p->vec_cols = p->width / vec;
-  p->vec_group = p->group_width / vec;
-  if (n == 0) {
-    p->threads = 32;
-    p->tile_cols = 1;
-    p->tile_rows = 1;
-    return KAT_OK;
-  }
-  if (p->vec_cols <= max_cols) {
-    p->tile_cols = int32_t(p->vec_cols);
-  } else {
-    const int64_t ncb = (p->vec_cols + max_cols - 1) / max_cols;
-    int64_t tcols = (p->vec_cols + ncb - 1) / ncb;
-    tcols = (tcols + 31) / 32 * 32;
-    if (tcols > max_cols) tcols = max_cols;
-    p->tile_cols = int32_t(tcols);
-  }
-  {
-    int64_t tr = max_threads / p->tile_cols;
-    if (tr > batch) tr = batch;
-    if (tr < 1) tr = 1;
-    p->tile_rows = int32_t(tr);
-  }
-  const int64_t used = int64_t(p->tile_cols) * p->tile_rows;
-  p->threads = int32_t((used + 31) / 32 * 32);
-  p->col_blocks = (p->vec_cols + p->tile_cols - 1) / p->tile_cols;
-  p->items = p->col_blocks * batch;
-  int64_t blocks = int64_t(sm_count) * ctas_per_sm;
-  if (blocks > kMaxBlocks) blocks = kMaxBlocks;
-  if (blocks > p->items) blocks = p->items;
-  p->blocks = blocks;
-  const int64_t per_block = (p->items + blocks - 1) / blocks;
-  int64_t segs = (per_block - 1) / batch + 2;
-  if (segs > p->col_blocks) segs = p->col_blocks;
-  p->max_segments = int32_t(segs);
-  int64_t lg = (int64_t(p->tile_cols) - 1) / p->vec_group + 2;
-  if (lg > num_groups) lg = num_groups;
-  p->max_local_groups = int32_t(lg);
-  p->workspace_bytes = uint64_t(blocks) * uint64_t(segs) * uint64_t(lg) * kAcc * sizeof(double);
-  p->items_q = p->items / blocks;
-  p->items_r = p->items % blocks;
-  make_divider(uint64_t(batch), &p->rows_m, &p->rows_s1, &p->rows_s2);
-  make_divider(uint64_t(p->vec_group), &p->vg_m, &p->vg_s1, &p->vg_s2);
-  return KAT_OK;
 }
 
 void to_public(const Plan& p, kat_rational_plan* out) {
