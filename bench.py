@@ -125,6 +125,51 @@ def init_process_group(world, rank, local):
     return dist
 
 
+def bind_to_gpu_numa(local: int) -> dict:
+    """Restrict this process to the host CPUs next to GPU `local` (its PCI device's NUMA
+    node), so that pinned host buffers allocated afterwards land in that node's memory.
+    Returns what was found: node, CPU count and PCI address (or the reason it is unknown)."""
+    try:
+        props = torch.cuda.get_device_properties(local)
+        bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        base = f"/sys/bus/pci/devices/{bus}"
+        with open(base + "/numa_node") as fh:
+            node = int(fh.read().strip())
+        cpus = set()
+        with open(base + "/local_cpulist") as fh:
+            for part in fh.read().strip().split(","):
+                if "-" in part:
+                    lo, hi = part.split("-")
+                    cpus.update(range(int(lo), int(hi) + 1))
+                elif part:
+                    cpus.add(int(part))
+        usable = cpus & os.sched_getaffinity(0)
+        if usable:
+            os.sched_setaffinity(0, usable)
+        return {"numa_node": node, "cpus": len(usable), "pci": bus}
+    except Exception as e:  # no sysfs entry (containers, other platforms)
+        return {"numa_node": None, "reason": f"{type(e).__name__}: {str(e)[:80]}"}
+
+
+def host_link_gbs(dev, host: torch.Tensor, stream) -> dict:
+    """H2D and D2H rates of one pinned host tensor's size on this rank (CUDA events)."""
+    d = torch.empty(host.shape, dtype=host.dtype, device=dev)
+    out = {}
+    for name, fn in (("h2d_GBps", lambda: d.copy_(host, non_blocking=True)),
+                     ("d2h_GBps", lambda: host.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(3):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        out[name] = 3 * host.numel() * host.element_size() / (a.elapsed_time(b) * 1e-3) / 1e9
+    del d
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Clock sampling (nvidia-smi while the GPU works)
 # ---------------------------------------------------------------------------
@@ -489,6 +534,7 @@ def run_ours(args):
     # the coefficient gradients back in pinned host memory, copies overlapped with compute.
     from rational_kat_cu_b200.host_io import HostPipeline
 
+    numa = bind_to_gpu_numa(local)
     h_x = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
     h_gy = torch.empty(w.shape, dtype=x.dtype, pin_memory=True)
     h_x.copy_(xs.cpu())
@@ -501,13 +547,15 @@ def run_ours(args):
 
     def e2e_step():
         mod.zero_grad(set_to_none=True)
-        if dist is not None:
+        if eager_exchange:
             pipe.run(h_x, h_gy, h_y, h_dx, wait=False)
             pipe.wait_compute()
             kdist.allreduce_coefficient_grads(mod)
             h_grads[0].copy_(mod.weight_numerator.grad, non_blocking=True)
             h_grads[1].copy_(mod.weight_denominator.grad, non_blocking=True)
         else:
+            # data parallel: the pipeline exchanges the gradients through the module's
+            # NVLink exchange buffers (no NCCL call)
             pipe.run(h_x, h_gy, h_y, h_dx, grads_host=h_grads, wait=False)
 
     for _ in range(2):
@@ -530,6 +578,12 @@ def run_ours(args):
         e_ms = float(t.item())
     e2e_ms_step = e_ms / args.e2e_steps
     e2e_value = world * N / (e2e_ms_step * 1e-3) / 1e9
+    link = host_link_gbs(dev, h_x, stream)
+    if dist is not None:
+        rates = [None] * world
+        dist.all_gather_object(rates, dict(link, **numa))
+    else:
+        rates = [dict(link, **numa)]
     h2d = 2 * N * elem_bytes
     d2h = 2 * N * elem_bytes + sum(h.numel() for h in h_grads) * 4
 
@@ -605,7 +659,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms_step,
                     "api": f"rational_kat_cu_b200.host_io.HostPipeline ({args.e2e_chunks} "
                            f"row chunks, H2D / compute / D2H overlapped, consecutive steps "
-                           f"overlapped)"},
+                           f"overlapped)",
+                    "per_rank_host": rates},
             "gpu_launches": launches_per_step * args.steps * world,
             "cpu_baseline": cpu,
             "clocks": clocks,

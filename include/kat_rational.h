@@ -251,6 +251,22 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
                                int64_t num_groups, int dtype,
                                const kat_rational_peers* peers, void* stream);
 
+/*
+ * The exchange step alone, for callers that reduce their coefficient gradients themselves (the
+ * host-buffer pipeline sums its row chunks' gradients first): grad_numerator [num_groups, 6]
+ * and grad_denominator [num_groups, 4] (fp32, this rank's gradients, device memory) are
+ * replaced in place by the rank-order fp64 sum over every rank of `peers` (divided by
+ * world_size when peers->average), rounded once to fp32, the same bits on every rank.  It
+ * shares the exchange buffers, the epoch counter and the fail-stop rules of
+ * kat_rational_bwd_allreduce: each call of either entry point is one exchange, and every rank
+ * makes the same sequence of calls.  On failure the gradients become NaN and the status word
+ * reads KAT_DEVICE_EXCHANGE_TIMEOUT.  Replaces the reference's (absent) distributed layer; no
+ * counterpart there.
+ */
+int kat_rational_exchange_grads(float* grad_numerator, float* grad_denominator,
+                                int64_t num_groups, const kat_rational_peers* peers,
+                                void* stream);
+
 /* Human-readable text for a status code (static storage). */
 const char* kat_rational_strerror(int status);
 

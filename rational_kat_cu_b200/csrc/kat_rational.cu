@@ -896,20 +896,27 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
 // One block: (1) sums every (group, slot) over the blocks of this GPU exactly as
 // kat_bwd_reduce_kernel does; (2) stores the G x 10 fp64 sums into every rank's exchange
 // buffer (peer memory, NVLink stores), into the row of this rank in the half selected by
-// the call's epoch parity; (3) raises this rank's flag on every rank (system-scope
-// release after a system fence); (4) waits, bounded by a wall-clock limit, until every
-// rank's flag on this GPU reached the epoch (system-scope acquire); (5) adds the ranks in
-// rank order in fp64 (optionally divided by the world size) and writes d_num / d_den.  All
-// ranks add the same numbers in the same order, so their gradients are bit-identical.
+// the call's epoch parity; (3) waits, bounded by a wall-clock limit, until every rank's row on
+// this GPU carries this call's tag; (4) adds the ranks in rank order in fp64 (optionally
+// divided by the world size) and writes d_num / d_den.  All ranks add the same numbers in
+// the same order, so their gradients are bit-identical.
+//
+// Tagged words.  Each fp64 sum travels as two 8-byte words, each holding 32 bits of the value
+// and the 32-bit tag of the call (the low half of its epoch).  An aligned 8-byte store is
+// single-copy atomic, so a reader sees a word either before the store or whole after it: a
+// word with the right tag carries the right data.  No fence and no separate flag are needed,
+// and every thread of the block waits for its own words in parallel (relaxed system-scope
+// stores and loads).
+//
 // The epoch is a per-buffer counter the kernel increments, so calls must be made the same
 // number of times on every rank (each rank's k-th call pairs with every other rank's k-th
-// call).  Two epoch halves let a rank run ahead by one call without overwriting data a
-// peer still reads: a rank can post call e + 1 only after it saw every flag reach e, and
-// call e + 2 only after every rank posted e + 1, which a rank does only once it has read
-// its call-e inbox.
+// call).  Two epoch halves let a rank run ahead by one call without overwriting data a peer
+// still reads: a rank can post call e + 1 only after it saw every row of call e, and call
+// e + 2 only after every rank posted e + 1, which a rank does only once it has read its call-e
+// inbox.  So a word of the half being read carries the tag of call e or of call e - 2 (not yet
+// overwritten); any other tag means the pairing broke.
 //
-// Failure is fail-stop.  A wait that runs out (or a flag seen more than one call ahead,
-// which the pairing above rules out unless some rank already gave up) sets
+// Failure is fail-stop.  A wait that runs out, or a word with a tag out of step, sets
 // KAT_DEVICE_EXCHANGE_TIMEOUT in the device status word, writes NaN gradients and sets this
 // rank's `broken` word; every later call on a broken buffer writes NaN at once and stores
 // nothing to any peer.  A rank that gave up therefore never posts again, so a late peer can
@@ -919,8 +926,8 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
 // stays broken until it is rebuilt.
 //
 // Exchange buffer layout (every rank, zero-initialised once):
-//   [0]    u64 epoch     [8] u64 broken     [64]  u64 flags[kMaxPeers] (flag[src] = epoch)
-//   [128]  f64 inbox[2][kMaxPeers][G][10]
+//   [0]    u64 epoch     [8] u64 broken
+//   [128]  u64 inbox[2][kMaxPeers][G * 10 * 2]   word = tag << 32 | 32 bits of a sum
 // ---------------------------------------------------------------------------
 
 constexpr int kMaxPeers = 8;
@@ -935,12 +942,12 @@ struct Peers {
   char* buf[kMaxPeers];
 };
 
-__device__ __forceinline__ void st_release_sys(uint64_t* ptr, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint64_t* ptr, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* ptr) {
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t* ptr) {
   uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
   return v;
 }
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -949,21 +956,97 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// The exchange itself, called by every thread of one block: s_sum[0 .. n_out) holds this
+// rank's sums on entry and the rank-order fp64 sums over all ranks on return (true), or the
+// call failed (false: timeout, tag out of step or a broken buffer; the status word is set).
+__device__ bool exchange_rows(double* s_sum, int n_out, const Peers& peers) {
+  __shared__ uint64_t s_epoch;
+  __shared__ int s_ok;
+  __shared__ volatile int s_fail;
+  const int tid = threadIdx.x;
+  const int n_words = 2 * n_out;      // tagged words per rank row
+  char* const own = peers.buf[peers.rank];
+  uint64_t* const broken = reinterpret_cast<uint64_t*>(own + 8);
+  if (tid == 0) {
+    uint64_t* ep = reinterpret_cast<uint64_t*>(own);
+    s_ok = *broken == 0 ? 1 : 0;
+    s_fail = 0;
+    s_epoch = *ep + 1;
+    if (s_ok) *ep = s_epoch;
+    else atomicExch(&g_kat_status, kStatusExchangeTimeout);
+  }
+  __syncthreads();
+  const uint64_t epoch = s_epoch;
+  const uint32_t tag = uint32_t(epoch);
+  const uint32_t stale = uint32_t(epoch - 2);   // the tag this half held before (0 = never written)
+  const int64_t half_words = int64_t(kMaxPeers) * n_words;
+  const int64_t inbox_words = 2 * half_words;
+  const size_t half = size_t(epoch & 1u);
+  const uint64_t* mine = reinterpret_cast<const uint64_t*>(own + kExchangeHeader) +
+                         half * half_words;
+  if (s_ok) {
+    // this rank's row into every rank's inbox: value bits low / high with the tag
+    for (int r = 0; r < peers.world; ++r) {
+      uint64_t* inbox = reinterpret_cast<uint64_t*>(peers.buf[r] + kExchangeHeader);
+      uint64_t* dst = inbox + half * half_words + int64_t(peers.rank) * n_words;
+      if (!in_bounds(inbox, inbox_words, dst, n_words)) continue;
+      for (int i = tid; i < n_words; i += blockDim.x) {
+        const uint64_t bits = uint64_t(__double_as_longlong(s_sum[i >> 1]));
+        const uint32_t word = (i & 1) ? uint32_t(bits >> 32) : uint32_t(bits);
+        st_relaxed_sys(dst + i, (uint64_t(tag) << 32) | word);
+      }
+    }
+    // every word of every rank's row of this half carries this call's tag
+    const uint64_t limit = uint64_t(peers.timeout_ms) * 1000000ull;
+    const uint64_t t0 = global_timer_ns();
+    const int total = peers.world * n_words;
+    for (int j = tid; j < total && !s_fail; j += blockDim.x) {
+      const uint64_t* w = mine + j;   // rank j / n_words, word j % n_words (rows adjacent)
+      for (;;) {
+        const uint32_t t = uint32_t(ld_relaxed_sys(w) >> 32);
+        if (t == tag) break;
+        const bool in_step = t == stale || (epoch <= 2 && t == 0);
+        if (!in_step || s_fail || global_timer_ns() - t0 > limit) {
+          s_fail = 1;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+  }
+  __syncthreads();   // every thread is done with its own row and with the waits
+  const bool ok = s_ok && !s_fail;
+  if (tid == 0 && s_ok && s_fail) {
+    *broken = 1;
+    atomicExch(&g_kat_status, kStatusExchangeTimeout);
+  }
+  if (ok) {
+    // ranks added in rank order, in fp64
+    for (int i = tid; i < n_out; i += blockDim.x) {
+      double v = 0.0;
+      for (int q = 0; q < peers.world; ++q) {
+        const uint64_t* row = mine + int64_t(q) * n_words;
+        const uint64_t lo = ld_relaxed_sys(row + 2 * i) & 0xffffffffull;
+        const uint64_t hi = ld_relaxed_sys(row + 2 * i + 1) & 0xffffffffull;
+        v += __longlong_as_double((long long)(lo | (hi << 32)));
+      }
+      s_sum[i] = v;
+    }
+  }
+  __syncthreads();
+  return ok;
+}
+
 __global__ void __launch_bounds__(kReduceThreads, 1)
 kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* __restrict__ den,
                                float* __restrict__ dnum, float* __restrict__ dden, const Plan p,
                                const Peers peers) {
   extern __shared__ double s_sum[];   // [G * 10]
-  __shared__ uint64_t s_epoch;
-  __shared__ int s_ok;
   const int G = int(p.num_groups);
-  const int n_out = G * kAcc;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nwarps = blockDim.x >> 5;
-  char* const own = peers.buf[peers.rank];
-  uint64_t* const broken = reinterpret_cast<uint64_t*>(own + 8);
   // Programmatic dependent of the partial-sum kernel, as kat_bwd_reduce_kernel.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int g = warp; g < G; g += nwarps) {
@@ -973,65 +1056,36 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
     for (int k = 0; k < kAcc; ++k)
       if (lane == k) s_sum[g * kAcc + k] = tot[k];
   }
-  if (tid == 0) {
-    uint64_t* ep = reinterpret_cast<uint64_t*>(own);
-    s_ok = *broken == 0 ? 1 : 0;
-    s_epoch = *ep + 1;
-    if (s_ok) *ep = s_epoch;
-    else atomicExch(&g_kat_status, kStatusExchangeTimeout);
-  }
   __syncthreads();
-  const uint64_t epoch = s_epoch;
-  const size_t half = size_t(epoch & 1u) * kMaxPeers;
-  if (s_ok) {
-    for (int r = 0; r < peers.world; ++r) {
-      double* inbox = reinterpret_cast<double*>(peers.buf[r] + kExchangeHeader);
-      double* dst = inbox + (half + size_t(peers.rank)) * size_t(n_out);
-      if (!in_bounds(inbox, int64_t(2) * kMaxPeers * n_out, dst, n_out)) continue;
-      for (int i = tid; i < n_out; i += blockDim.x) dst[i] = s_sum[i];
-    }
-  }
-  __syncthreads();
-  if (tid == 0 && s_ok) {
-    __threadfence_system();
-    for (int r = 0; r < peers.world; ++r)
-      st_release_sys(reinterpret_cast<uint64_t*>(peers.buf[r] + 64) + peers.rank, epoch);
-    const uint64_t* flags = reinterpret_cast<const uint64_t*>(own + 64);
-    const uint64_t limit = uint64_t(peers.timeout_ms) * 1000000ull;
-    const uint64_t t0 = global_timer_ns();
-    int ok = 1;
-    for (int q = 0; q < peers.world && ok; ++q) {
-      uint64_t f;
-      while ((f = ld_acquire_sys(flags + q)) < epoch) {
-        if (global_timer_ns() - t0 > limit) {
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
-      if (ok && f > epoch + 1) ok = 0;   // out of step: some rank already gave up
-    }
-    if (!ok) {
-      *broken = 1;
-      atomicExch(&g_kat_status, kStatusExchangeTimeout);
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  const double* inbox = reinterpret_cast<const double*>(own + kExchangeHeader) +
-                        half * size_t(n_out);
+  const bool ok = exchange_rows(s_sum, G * kAcc, peers);
   const double scale = peers.average ? 1.0 / double(peers.world) : 1.0;
-  const bool ok = s_ok != 0;
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
 #pragma unroll
-    for (int k = 0; k < kAcc; ++k) {
-      double v = 0.0;
-      if (ok)
-        for (int q = 0; q < peers.world; ++q) v += inbox[size_t(q) * n_out + g * kAcc + k];
-      tot[k] = v;
-    }
+    for (int k = 0; k < kAcc; ++k) tot[k] = s_sum[g * kAcc + k];
     write_group(tot, scale, ok, g, lane, den, dnum, dden, p.formula);
+  }
+}
+
+// Exchange-only call: this rank's final coefficient gradients (fp32, [G, 6] and [G, 4]) in,
+// the rank-order fp64 sum over all ranks (optionally averaged), rounded once, out (in place).
+__global__ void __launch_bounds__(kReduceThreads, 1)
+kat_exchange_grads_kernel(float* __restrict__ dnum, float* __restrict__ dden, int G,
+                          const Peers peers) {
+  extern __shared__ double s_sum[];   // [G * 10]: d_num row g then d_den row g
+  const int n_out = G * kAcc;
+  for (int i = threadIdx.x; i < n_out; i += blockDim.x) {
+    const int g = i / kAcc, k = i - g * kAcc;
+    s_sum[i] = double(k < 6 ? dnum[g * 6 + k] : dden[g * 4 + (k - 6)]);
+  }
+  __syncthreads();
+  const bool ok = exchange_rows(s_sum, n_out, peers);
+  const double scale = peers.average ? 1.0 / double(peers.world) : 1.0;
+  for (int i = threadIdx.x; i < n_out; i += blockDim.x) {
+    const int g = i / kAcc, k = i - g * kAcc;
+    const float f = ok ? float(s_sum[i] * scale) : __int_as_float(0x7fc00000);
+    if (k < 6) dnum[g * 6 + k] = f;
+    else dden[g * 4 + (k - 6)] = f;
   }
 }
 
@@ -2065,7 +2119,7 @@ int kat_rational_enable_peer_access(int device, int peer_device) {
 int kat_rational_exchange_create(int64_t num_groups, void** buffer, void* ipc_handle) {
   if (buffer == nullptr || ipc_handle == nullptr) return KAT_ERR_NULL_POINTER;
   if (num_groups < 1) return KAT_ERR_BAD_GROUPS;
-  const size_t bytes = kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * 8;
+  const size_t bytes = kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * 16;
   void* p = nullptr;
   if (cudaMalloc(&p, bytes) != cudaSuccess) return KAT_ERR_CUDA;
   cudaIpcMemHandle_t h;
@@ -2108,8 +2162,37 @@ int kat_rational_exchange_destroy(void* buffer) {
 
 size_t kat_rational_exchange_buffer_bytes(int64_t num_groups) {
   if (num_groups < 1) return 0;
-  return kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * sizeof(double);
+  return kExchangeHeader + size_t(2) * kMaxPeers * size_t(num_groups) * kAcc * 16;
 }
+
+}  // extern "C"
+
+namespace {
+
+// Checks a kat_rational_peers descriptor and copies it into the kernels' form.
+int peers_from(const kat_rational_peers* peers, int64_t num_groups, Peers* pe) {
+  if (peers == nullptr) return KAT_ERR_NULL_POINTER;
+  if (peers->world_size < 1 || peers->world_size > KAT_MAX_PEERS || peers->rank < 0 ||
+      peers->rank >= peers->world_size || peers->timeout_ms < 1)
+    return KAT_ERR_BAD_SHAPE;
+  if (num_groups < 1 || num_groups * kAcc * int64_t(sizeof(double)) > 200 * 1024)
+    return KAT_ERR_BAD_GROUPS;
+  memset(pe, 0, sizeof(*pe));
+  pe->world = peers->world_size;
+  pe->rank = peers->rank;
+  pe->average = peers->average ? 1 : 0;
+  pe->timeout_ms = peers->timeout_ms;
+  for (int r = 0; r < pe->world; ++r) {
+    if (peers->buffers[r] == nullptr || (reinterpret_cast<uintptr_t>(peers->buffers[r]) % 16) != 0)
+      return KAT_ERR_NULL_POINTER;
+    pe->buf[r] = static_cast<char*>(peers->buffers[r]);
+  }
+  return KAT_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x,
                                const float* numerator, const float* denominator,
@@ -2117,26 +2200,29 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
                                size_t workspace_bytes, int64_t batch, int64_t channels,
                                int64_t inner, int64_t num_groups, int dtype,
                                const kat_rational_peers* peers, void* stream) {
-  if (peers == nullptr) return KAT_ERR_NULL_POINTER;
-  if (peers->world_size < 1 || peers->world_size > KAT_MAX_PEERS || peers->rank < 0 ||
-      peers->rank >= peers->world_size || peers->timeout_ms < 1)
-    return KAT_ERR_BAD_SHAPE;
-  if (num_groups < 1 || num_groups * kAcc * int64_t(sizeof(double)) > 200 * 1024)
-    return KAT_ERR_BAD_GROUPS;
   Peers pe;
-  memset(&pe, 0, sizeof(pe));
-  pe.world = peers->world_size;
-  pe.rank = peers->rank;
-  pe.average = peers->average ? 1 : 0;
-  pe.timeout_ms = peers->timeout_ms;
-  for (int r = 0; r < pe.world; ++r) {
-    if (peers->buffers[r] == nullptr || (reinterpret_cast<uintptr_t>(peers->buffers[r]) % 16) != 0)
-      return KAT_ERR_NULL_POINTER;
-    pe.buf[r] = static_cast<char*>(peers->buffers[r]);
-  }
+  const int st = peers_from(peers, num_groups, &pe);
+  if (st != KAT_OK) return st;
   return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
                   workspace, workspace_bytes, batch, channels, inner, num_groups, dtype,
                   kFormulaKat, stream, &pe);
+}
+
+int kat_rational_exchange_grads(float* grad_numerator, float* grad_denominator,
+                                int64_t num_groups, const kat_rational_peers* peers,
+                                void* stream) {
+  if (grad_numerator == nullptr || grad_denominator == nullptr) return KAT_ERR_NULL_POINTER;
+  Peers pe;
+  const int st = peers_from(peers, num_groups, &pe);
+  if (st != KAT_OK) return st;
+  const size_t smem = size_t(num_groups) * kAcc * sizeof(double);
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute((const void*)kat_exchange_grads_kernel,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return KAT_ERR_CUDA;
+  kat_exchange_grads_kernel<<<1, kReduceThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      grad_numerator, grad_denominator, int(num_groups), pe);
+  return cudaGetLastError() == cudaSuccess ? KAT_OK : KAT_ERR_CUDA;
 }
 
 }  // extern "C"

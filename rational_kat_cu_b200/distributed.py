@@ -135,6 +135,7 @@ class PeerExchange:
         self._local = None
         self.group = group
         self.device = device
+        self.peers_groups = int(num_groups)
         with torch.cuda.device(device):
             local = ctypes.c_void_p()
             handle = (ctypes.c_char * 64)()
@@ -165,6 +166,22 @@ class PeerExchange:
         for r, ptr in enumerate(ptrs):
             self.peers.buffers[r] = ctypes.c_void_p(ptr)
         dist.barrier(group=group)
+
+    def exchange_grads(self, grad_numerator: torch.Tensor, grad_denominator: torch.Tensor,
+                       stream: Optional[torch.cuda.Stream] = None) -> None:
+        """In place: this rank's fp32 coefficient gradients [G, 6] and [G, 4] become the
+        rank-order sum (or average) over all ranks, through the same buffers and epoch as the
+        fused backward (kat_rational_exchange_grads).  Enqueued on `stream` (default: current);
+        every rank must make the same sequence of exchanges."""
+        for t, cols in ((grad_numerator, 6), (grad_denominator, 4)):
+            if (t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.device or
+                    t.shape != (self.peers_groups, cols)):
+                raise ValueError(f"exchange_grads expects contiguous fp32 [{self.peers_groups}, "
+                                 f"{cols}] tensors on {self.device}")
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        _native.check("kat_rational_exchange_grads", self._lib.kat_rational_exchange_grads(
+            grad_numerator.data_ptr(), grad_denominator.data_ptr(), self.peers_groups,
+            ctypes.byref(self.peers), ctypes.c_void_p(s.cuda_stream)))
 
     def close(self) -> None:
         """Collective teardown: every rank of the group must call it, after its last use.

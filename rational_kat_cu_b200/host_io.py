@@ -11,8 +11,9 @@ H2D and D2H use the two directions of the link at the same time, so a step costs
 larger of the two transfers instead of their sum.  The kernels are driven through the C ABI
 with preallocated per-slot device buffers (no autograd work per chunk); each chunk's
 coefficient gradients land in their own row of a [chunks, G, 10] buffer, summed once per
-step in chunk order and added to the module's .grad — deterministic for a fixed chunk
-count.  The reference has no host-buffer API; this is the B200 design's way to feed the
+step in chunk order (exchanged with the other ranks when the module is data parallel, see
+KAT_Group.enable_data_parallel) and added to the module's .grad — deterministic for a fixed
+chunk count.  The reference has no host-buffer API; this is the B200 design's way to feed the
 kernels from host memory.
 """
 
@@ -164,8 +165,14 @@ class HostPipeline:
                 ev_out[k].record(self.d2h)
             used[k] = True
         with torch.cuda.stream(self.comp):
-            d_num = st["dn"][:len(bounds)].sum(dim=(0, 1)).view(1, 6)
-            d_den = st["dd"][:len(bounds)].sum(dim=0)
+            dn_g = st["dn"][:len(bounds)].sum(dim=0)     # [G, 6], chunks in order
+            d_den = st["dd"][:len(bounds)].sum(dim=0)    # [G, 4]
+            exchange = getattr(mod, "exchange", None)
+            if exchange is not None:
+                # data parallel (KAT_Group.enable_data_parallel): the rank-order sum over the
+                # ranks, through the module's NVLink exchange buffers
+                exchange.exchange_grads(dn_g, d_den, self.comp)
+            d_num = dn_g.sum(dim=0).view(1, 6)
             for p, g in ((mod.weight_numerator, d_num), (mod.weight_denominator, d_den)):
                 g = g.reshape(p.shape).to(p.dtype)
                 if p.grad is None:

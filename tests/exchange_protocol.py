@@ -6,47 +6,72 @@ has this GPU's G x 10 fp64 sums, so the protocol can be run on the CPU with simu
 (threads) and any interleaving a test forces:
 
   1. a buffer marked broken by an earlier failure: NaN at once, nothing stored anywhere;
-  2. epoch = own epoch + 1 (kernel-owned counter); half = epoch & 1;
-  3. store this rank's sums into row `rank` of that half in every rank's inbox;
-  4. raise flag[rank] = epoch on every rank (the kernel: system fence, then release stores);
-  5. wait, bounded by the timeout, until every flag on this rank is >= epoch (acquire
-     loads); a flag more than one epoch ahead is out of step;
-  6. on a timeout or out-of-step flag: mark the own buffer broken and return NaN;
-  7. otherwise add the ranks' rows of this half in rank order in float64.
+  2. epoch = own epoch + 1 (kernel-owned counter); tag = epoch mod 2^32; half = epoch & 1;
+  3. store this rank's sums into row `rank` of that half in every rank's inbox, each fp64
+     as two words (tag, low 32 bits) and (tag, high 32 bits) — one word is one single-copy
+     atomic 8-byte store on the GPU, one tuple assignment here;
+  4. wait, bounded by the timeout, until every word of every row of the half on this rank
+     carries the tag; a word may meanwhile only carry the tag of call epoch - 2 (or 0 before
+     the first two calls): any other tag is out of step;
+  5. on a timeout or a tag out of step: mark the own buffer broken and return NaN;
+  6. otherwise decode the rows and add them in rank order in float64.
 
 Ranks here share one address space and the GIL orders every access, which is at least as
-strong as the kernel's release/acquire pairs.  `Variant` plants protocol mistakes (one
-inbox half instead of two; no broken word and no out-of-step check) so the tests can show
-they would be caught.  Nothing in the product imports this file.
+strong as the kernel's relaxed system-scope word stores and loads.  `Variant` plants
+protocol mistakes (one inbox half instead of two; no fail-stop and no step check; only the
+first word of a row checked, as a single flag would be) so the tests can show they would be
+caught.  Nothing in the product imports this file.
 """
 
 from __future__ import annotations
 
 import dataclasses
+import struct
 import threading
 import time
-from typing import Callable, Dict, List, Optional
+from typing import Callable, Dict, List, Optional, Tuple
 
 import numpy as np
 
 MAX_PEERS = 8
 NAN = float("nan")
+MASK32 = 0xFFFFFFFF
 
 
 @dataclasses.dataclass
 class Variant:
-    halves: int = 2            # 1 plants the overwrite race the two halves prevent
-    fail_stop: bool = True     # False plants "keep posting after a timeout, no step check"
+    halves: int = 2             # 1 plants the overwrite race the two halves prevent
+    fail_stop: bool = True      # False plants "keep posting after a timeout, no step check"
+    every_word: bool = True     # False plants "wait for the first word of a row only"
+
+
+Word = Tuple[int, int]          # (tag, 32 payload bits)
+
+
+def encode(values: np.ndarray, tag: int) -> List[Word]:
+    words: List[Word] = []
+    for v in values:
+        bits = struct.unpack("<Q", struct.pack("<d", float(v)))[0]
+        words.append((tag, bits & MASK32))
+        words.append((tag, bits >> 32))
+    return words
+
+
+def decode(words: List[Word]) -> np.ndarray:
+    out = np.empty(len(words) // 2, dtype=np.float64)
+    for i in range(out.shape[0]):
+        bits = words[2 * i][1] | (words[2 * i + 1][1] << 32)
+        out[i] = struct.unpack("<d", struct.pack("<Q", bits))[0]
+    return out
 
 
 class ExchangeBuffer:
-    """One rank's exchange buffer: epoch, broken word, flags[MAX_PEERS], inbox[2][peers][n]."""
+    """One rank's exchange buffer: epoch, broken word, inbox[2][MAX_PEERS][2n] words."""
 
     def __init__(self, n: int):
         self.epoch = 0
         self.broken = 0
-        self.flags = [0] * MAX_PEERS
-        self.inbox = np.zeros((2, MAX_PEERS, n), dtype=np.float64)
+        self.inbox = [[[(0, 0)] * (2 * n) for _ in range(MAX_PEERS)] for _ in range(2)]
         self.stores_from: List[int] = []   # ranks that stored into this buffer, in order
 
 
@@ -57,14 +82,14 @@ class Status:
         self.value = 0
 
 
-Hook = Callable[[int, int, str, int], None]   # (rank, epoch, point, peer)
+Hook = Callable[[int, int, str, int], None]   # (rank, epoch, point, peer or word index)
 
 
 def exchange_call(rank: int, world: int, bufs: List[ExchangeBuffer], sums: np.ndarray,
                   timeout_s: float, status: Status, hook: Optional[Hook] = None,
                   variant: Variant = Variant(), poll_s: float = 1e-4) -> np.ndarray:
     """One call of the exchange on rank `rank`; returns the rank-order float64 totals, or an
-    all-NaN vector when the call failed (steps 1-7 above)."""
+    all-NaN vector when the call failed (steps 1-6 above)."""
     hook = hook or (lambda *a: None)
     own = bufs[rank]
     n = sums.shape[0]
@@ -73,28 +98,35 @@ def exchange_call(rank: int, world: int, bufs: List[ExchangeBuffer], sums: np.nd
         return np.full(n, NAN)
     own.epoch += 1
     epoch = own.epoch
+    tag = epoch & MASK32
+    stale = (epoch - 2) & MASK32
     half = epoch & 1 if variant.halves == 2 else 0
+    words = encode(sums, tag)
     for r in range(world):
         hook(rank, epoch, "store", r)
-        bufs[r].inbox[half, rank, :] = sums
+        row = bufs[r].inbox[half][rank]
+        for i, w in enumerate(words):
+            if i == len(words) // 2:
+                hook(rank, epoch, "store_mid", r)
+            row[i] = w
         bufs[r].stores_from.append(rank)
     hook(rank, epoch, "stored", -1)
-    for r in range(world):
-        bufs[r].flags[rank] = epoch
-    hook(rank, epoch, "flagged", -1)
     t0 = time.monotonic()
     ok = True
     for q in range(world):
-        while True:
-            f = own.flags[q]
-            if f >= epoch:
+        row = own.inbox[half][q]
+        for i in range(2 * n if variant.every_word else 1):
+            while True:
+                t = row[i][0]
+                if t == tag:
+                    break
+                in_step = t == stale or (epoch <= 2 and t == 0) or not variant.fail_stop
+                if not in_step or time.monotonic() - t0 > timeout_s:
+                    ok = False
+                    break
+                time.sleep(poll_s)
+            if not ok:
                 break
-            if time.monotonic() - t0 > timeout_s:
-                ok = False
-                break
-            time.sleep(poll_s)
-        if ok and variant.fail_stop and f > epoch + 1:
-            ok = False
         if not ok:
             break
     if not ok:
@@ -105,7 +137,7 @@ def exchange_call(rank: int, world: int, bufs: List[ExchangeBuffer], sums: np.nd
     tot = np.zeros(n, dtype=np.float64)
     for q in range(world):
         hook(rank, epoch, "read", q)
-        tot = tot + own.inbox[half, q, :]
+        tot = tot + decode(own.inbox[half][q])
     return tot
 
 
@@ -170,4 +202,4 @@ def classify(v: np.ndarray, world: int, call: int) -> str:
 
 
 __all__ = ["Variant", "ExchangeBuffer", "Status", "exchange_call", "contribution", "expected",
-           "run_ranks", "classify", "is_nan", "exact"]
+           "run_ranks", "classify", "is_nan", "exact", "encode", "decode"]

@@ -5,8 +5,8 @@ exchange fused into the reduction kernel over NVLink peer memory.
   - a wait that runs out (a second rank that never arrives: both "ranks" point at one
     buffer, so nothing ever raises rank 1's flag) sets KAT_DEVICE_EXCHANGE_TIMEOUT, writes
     NaN gradients, leaves dx intact and the context usable;
-  - a flag more than one call ahead is refused at once (NaN, status, broken buffer), and a
-    broken buffer fails the next call at once without posting anything;
+  - a word tagged with a call out of step is refused at once (NaN, status, broken buffer),
+    and a broken buffer fails the next call at once without posting anything;
   - with two GPUs, two processes get identical gradients equal to the rank-order average of
     their local gradients, then tear the buffers down collectively (skipped on one-GPU
     machines).
@@ -100,17 +100,20 @@ def test_missing_rank_times_out_with_status(cuda_device):
     assert _native.device_status(0) == 0
 
 
-def test_flag_far_ahead_is_refused_without_waiting(cuda_device):
-    """A peer flag more than one call ahead cannot come from a correct pairing: the call
-    writes NaN gradients, sets the status and marks the buffer broken, with no wait.
-    (Both "ranks" share one buffer; rank 1's flag is preset to 10.)"""
+def test_tag_out_of_step_is_refused_without_waiting(cuda_device):
+    """A peer word tagged with a call out of step (here call 10 where call 1 or none is
+    possible) cannot come from a correct pairing: the call writes NaN gradients, sets the
+    status and marks the buffer broken, with no wait.  (Both "ranks" share one buffer; the
+    first word of rank 1's row in the half of call 1 is preset.)"""
     lib = _native.lib()
     G = 8
     x, gy, n, d = _problem(cuda_device, G=G)
     buf = torch.zeros(lib.kat_rational_exchange_buffer_bytes(G), dtype=torch.uint8,
                       device=cuda_device)
     words = buf.view(torch.int64)
-    words[8 + 1] = 10                      # flags[1] (flags start at byte 64)
+    n_words = 2 * G * 10                   # tagged words per rank row
+    half_words = 8 * n_words               # rows of all KAT_MAX_PEERS ranks
+    words[16 + half_words + n_words] = 10 << 32   # inbox at byte 128; half 1, rank 1, word 0
     _native.device_status(0, reset=True)
     st, dx, dn, dd = _call(lib.kat_rational_bwd_allreduce, x, gy, n, d, G,
                            _peers([buf, buf], 0, timeout_ms=60000))
@@ -145,6 +148,45 @@ def test_broken_buffer_fails_at_once(cuda_device):
     assert int(words[0]) == 1              # no new epoch was posted
     assert _native.device_status(0, reset=True) == _native.KAT_DEVICE_EXCHANGE_TIMEOUT
     assert _native.device_status(0) == 0
+
+
+def test_exchange_grads_world_one_is_identity(cuda_device):
+    """kat_rational_exchange_grads at world size 1: the rank-order sum of one rank is its
+    own gradients, bit for bit, call after call (the epoch advances)."""
+    lib = _native.lib()
+    G = 8
+    buf = torch.zeros(lib.kat_rational_exchange_buffer_bytes(G), dtype=torch.uint8,
+                      device=cuda_device)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    for call in range(3):
+        dn = torch.randn(G, 6, generator=g).to(cuda_device)
+        dd = torch.randn(G, 4, generator=g).to(cuda_device)
+        dn0, dd0 = dn.clone(), dd.clone()
+        p = _peers([buf], 0)
+        st = lib.kat_rational_exchange_grads(dn.data_ptr(), dd.data_ptr(), G, ctypes.byref(p),
+                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert st == 0 and torch.equal(dn, dn0) and torch.equal(dd, dd0)
+    assert int(buf.view(torch.int64)[0]) == 3
+    assert _native.device_status(0) == 0
+
+
+def test_exchange_grads_missing_rank_gives_nan(cuda_device):
+    lib = _native.lib()
+    G = 4
+    buf = torch.zeros(lib.kat_rational_exchange_buffer_bytes(G), dtype=torch.uint8,
+                      device=cuda_device)
+    dn = torch.ones(G, 6, device=cuda_device)
+    dd = torch.ones(G, 4, device=cuda_device)
+    _native.device_status(0, reset=True)
+    p = _peers([buf, buf], 0, timeout_ms=50)
+    st = lib.kat_rational_exchange_grads(dn.data_ptr(), dd.data_ptr(), G, ctypes.byref(p),
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert st == 0 and torch.isnan(dn).all() and torch.isnan(dd).all()
+    assert _native.device_status(0, reset=True) == _native.KAT_DEVICE_EXCHANGE_TIMEOUT
+    assert lib.kat_rational_exchange_grads(None, dd.data_ptr(), G, ctypes.byref(p), None) == \
+        _native.KAT_ERR_NULL_POINTER
 
 
 def test_descriptor_validation():
@@ -192,6 +234,23 @@ for step in range(3):
     dist.all_gather(gots, got)
     assert all(torch.equal(gots[0], t) for t in gots), "ranks differ"
 from rational_kat_cu_b200 import _native
+from rational_kat_cu_b200.host_io import HostPipeline
+# the host-buffer pipeline of a data-parallel module exchanges through the same buffers
+hx = x.cpu().pin_memory(); hg = gy.cpu().pin_memory()
+hy = torch.empty_like(hx).pin_memory(); hdx = torch.empty_like(hx).pin_memory()
+for mod in (ref, m):
+    mod.zero_grad(set_to_none=True)
+    HostPipeline(mod, chunks=4).run(hx, hg, hy, hdx)
+torch.cuda.synchronize()
+local = torch.cat([ref.weight_numerator.grad.reshape(-1), ref.weight_denominator.grad.reshape(-1)])
+allg = [torch.empty_like(local) for _ in range(world)]
+dist.all_gather(allg, local)
+expect = sum(a.double() for a in allg) / world
+got = torch.cat([m.weight_numerator.grad.reshape(-1), m.weight_denominator.grad.reshape(-1)])
+torch.testing.assert_close(got.double(), expect, rtol=1e-5, atol=1e-5)
+gots = [torch.empty_like(got) for _ in range(world)]
+dist.all_gather(gots, got)
+assert all(torch.equal(gots[0], t) for t in gots), "pipeline ranks differ"
 assert _native.device_status(rank) == 0
 m.disable_data_parallel()      # collective teardown: unmap, barrier, free
 assert m.exchange is None
