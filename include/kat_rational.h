@@ -65,6 +65,14 @@ extern "C" {
 /* Denominator formulas (the *_formula entry points). */
 #define KAT_FORMULA_KAT 0      /* Q = 1 + sum_i |b_i| x^i       (kat_rational/kat_1dgroup_torch.py) */
 #define KAT_FORMULA_ABS_SUM 1  /* Q = 1 + |sum_i b_i x^i|       (rational_kat_cu rat_cuda) */
+/* Flag or-ed into `formula` of kat_rational_fwd_formula / kat_rational_bwd_formula: `numerator`
+ * is ONE row of 6 coefficients used by every group (the modules' weight_numerator [1, 6],
+ * which the reference repeats per group on every forward: kat_rational/kat_1dgroup_triton.py:86),
+ * and the backward writes grad_numerator as ONE row [6], the sum over groups of the per-group
+ * gradients (added in fp64 in a fixed order, rounded once) — the gradient the reference's
+ * repeat backward produces, without the repeat and the sum as separate launches.  Not accepted
+ * by the data-parallel entry points. */
+#define KAT_SHARED_NUMERATOR 0x100
 
 /*
  * Forward: y = P(x)/Q(x).

@@ -61,6 +61,7 @@ EXPORTED_SYMBOLS = (
     "kat_gemm_set_test_stall",
 )
 
+KAT_SHARED_NUMERATOR = 0x100
 KAT_MAX_PEERS = 8
 KAT_DEVICE_WAIT_TIMEOUT = 1
 KAT_DEVICE_EXCHANGE_TIMEOUT = 2

@@ -262,8 +262,8 @@ __device__ __forceinline__ float den_coef(const float* b, int i) {
 template <typename L, int kF>
 __device__ __forceinline__ void load_fwd_coef(const float* __restrict__ num,
                                               const float* __restrict__ den, int64_t g,
-                                              FwdCoef<L>& c) {
-  const float* a = num + g * 6;
+                                              FwdCoef<L>& c, int num_stride = 6) {
+  const float* a = num + g * num_stride;   // num_stride 0: one numerator row for every group
   const float* b = den + g * 4;
   c.a0 = bcast<L>(__ldg(a + 0)); c.a1 = bcast<L>(__ldg(a + 1)); c.a2 = bcast<L>(__ldg(a + 2));
   c.a3 = bcast<L>(__ldg(a + 3)); c.a4 = bcast<L>(__ldg(a + 4)); c.a5 = bcast<L>(__ldg(a + 5));
@@ -275,8 +275,8 @@ __device__ __forceinline__ void load_fwd_coef(const float* __restrict__ num,
 template <typename L, int kF>
 __device__ __forceinline__ void load_bwd_coef(const float* __restrict__ num,
                                               const float* __restrict__ den, int64_t g,
-                                              BwdCoef<L>& c) {
-  const float* a = num + g * 6;
+                                              BwdCoef<L>& c, int num_stride = 6) {
+  const float* a = num + g * num_stride;   // num_stride 0: one numerator row for every group
   const float* b = den + g * 4;
   c.a0 = bcast<L>(__ldg(a + 0)); c.a1 = bcast<L>(__ldg(a + 1)); c.a2 = bcast<L>(__ldg(a + 2));
   c.a3 = bcast<L>(__ldg(a + 3)); c.a4 = bcast<L>(__ldg(a + 4)); c.a5 = bcast<L>(__ldg(a + 5));

@@ -33,6 +33,7 @@ struct Plan {
   uint64_t vg_m;       // ... and by vec_group
   int32_t rows_s1, rows_s2, vg_s1, vg_s2;
   int32_t formula;     // KAT_FORMULA_*: how the reduction signs the denominator terms
+  int32_t num_stride;  // floats between groups' numerator rows: 6, or 0 for one shared row
 };
 
 // Division by an invariant divisor d >= 1 with a multiply and shifts (Granlund and

@@ -213,7 +213,7 @@ kat_fwd_kernel(const Tio* __restrict__ x, Tio* __restrict__ y,
     const int64_t r_end = seg_end - cb * p.rows;
     if (col < p.vec_cols && r0 < r_end) {
       FwdCoef<L> c;
-      load_fwd_coef<L, kF>(num, den, col / p.vec_group, c);
+      load_fwd_coef<L, kF>(num, den, col / p.vec_group, c, p.num_stride);
       const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
       const Tio* xp = x + r0 * p.width + col * V;
       Tio* yp = y + r0 * p.width + col * V;
@@ -280,7 +280,7 @@ kat_bwd_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* __res
     const int64_t r_end = seg_end - cb * p.rows;
     if (row_thread && col < p.vec_cols && r0 < r_end) {
       BwdCoef<L> c;
-      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c);
+      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c, p.num_stride);
       const int64_t n = (r_end - r0 + p.tile_rows - 1) / p.tile_rows;
       const int64_t off = r0 * p.width + col * V;
       const Tio* xp = x + off;
@@ -428,7 +428,7 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
     for (int k = 0; k < kAcc; ++k) acc[k] = bcast<L>(0.0f);
     if (row_thread && col < p.vec_cols && r0 < r_end) {
       BwdCoef<L> c;
-      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c);
+      load_bwd_coef<L, kF>(num, den, col / p.vec_group, c, p.num_stride);
       const int n = int(min(int64_t(0x7fffffff), (r_end - r0 + p.tile_rows - 1) / p.tile_rows));
       const int nb = (n + kRows - 1) / kRows;
       const int64_t off = r0 * p.width + col * V;
@@ -562,6 +562,45 @@ kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restric
   double tot[kAcc];
   group_totals(partial, p, g, lane, tot);
   write_group(tot, 1.0, true, g, lane, den, dnum, dden, p.formula);
+}
+
+// The same with one numerator row shared by every group: one block; warp w takes groups
+// w, w + 8, ... in order, writes their denominator gradients and adds their numerator totals;
+// the 8 warp sums are then added in warp order (fp64) and rounded once into dnum[0..5].
+__global__ void __launch_bounds__(kReduceWarps * 32)
+kat_bwd_reduce_shared_kernel(const double* __restrict__ partial, const float* __restrict__ den,
+                             float* __restrict__ dnum, float* __restrict__ dden, const Plan p) {
+  __shared__ double s_num[kReduceWarps][6];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  double num_sum = 0.0;   // lane k < 6: numerator moment k over this warp's groups
+  for (int64_t g = warp; g < p.num_groups; g += kReduceWarps) {
+    double tot[kAcc];
+    group_totals(partial, p, g, lane, tot);
+#pragma unroll
+    for (int k = 0; k < 6; ++k)
+      if (lane == k) num_sum += tot[k];
+    if (lane >= 6 && lane < kAcc) {
+      double v = 0.0;
+#pragma unroll
+      for (int k = 6; k < kAcc; ++k)
+        if (lane == k) v = tot[k];
+      float sg = 1.0f;
+      if (p.formula == kFormulaKat) {
+        const float b = den[g * 4 + (lane - 6)];
+        sg = b > 0.0f ? 1.0f : (b < 0.0f ? -1.0f : b * 0.0f);
+      }
+      dden[g * 4 + (lane - 6)] = -(sg * float(v));
+    }
+  }
+  if (lane < 6) s_num[warp][lane] = num_sum;
+  __syncthreads();
+  if (threadIdx.x < 6) {
+    double v = 0.0;
+    for (int w = 0; w < kReduceWarps; ++w) v += s_num[w][threadIdx.x];
+    dnum[threadIdx.x] = float(v);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -797,7 +836,7 @@ kat_fwd_tma_kernel(const Tio* __restrict__ x, Tio* __restrict__ y, const float* 
     const int64_t col = cb * p.tile_cols + tc;
     if (row_thread && col < p.vec_cols) {
       if (cb != cb_coef) {
-        load_fwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c);
+        load_fwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c, p.num_stride);
         cb_coef = cb;
       }
       const char* src = slots + size_t(s) * slot_bytes + size_t(tc) * 16;
@@ -861,7 +900,7 @@ kat_bwd_tma_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio* _
     const int64_t col = cb * p.tile_cols + tc;
     if (row_thread && col < p.vec_cols) {
       if (cb != cb_coef) {
-        load_bwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c);
+        load_bwd_coef<float2, kFormulaKat>(num, den, col / p.vec_group, c, p.num_stride);
         cb_coef = cb;
       }
       const char* xs = slots + (size_t(s) * 2) * slot_bytes + size_t(tc) * 16;
@@ -1742,7 +1781,11 @@ cudaError_t launch_bwd_tma(int dtype, const void* x, const void* gy, void* dx, c
 
 int launch_reduce(const void* workspace, const float* den, float* dnum, float* dden,
                   const Plan& p, const Peers* peers, cudaStream_t s) {
-  if (peers == nullptr) {
+  if (peers == nullptr && p.num_stride == 0) {
+    if (launch_pdl(kat_bwd_reduce_shared_kernel, dim3(1), dim3(kReduceWarps * 32), 0, s,
+                   static_cast<const double*>(workspace), den, dnum, dden, p) != cudaSuccess)
+      return KAT_ERR_CUDA;
+  } else if (peers == nullptr) {
     // Programmatic dependent launch: the reduction's launch overlaps the tail of the
     // partial-sum kernel, and griddepcontrol.wait inside it orders the reads.
     const unsigned grid = unsigned((p.num_groups + kReduceWarps - 1) / kReduceWarps);
@@ -1775,7 +1818,11 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
+  const bool shared = (formula & KAT_SHARED_NUMERATOR) != 0;
+  formula &= ~KAT_SHARED_NUMERATOR;
   if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
+  if (shared && peers != nullptr) return KAT_ERR_BAD_FORMULA;
+  const int num_stride = shared ? 0 : 6;
   if (numerator == nullptr || denominator == nullptr || grad_numerator == nullptr ||
       grad_denominator == nullptr)
     return KAT_ERR_NULL_POINTER;
@@ -1795,6 +1842,7 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
       if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
           (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
         return KAT_ERR_WORKSPACE;
+      p.num_stride = num_stride;
       if (launch_bwd_async(dtype, formula, x, grad_out, grad_x, numerator, denominator,
                            static_cast<double*>(workspace), p, s) != cudaSuccess)
         return KAT_ERR_CUDA;
@@ -1814,6 +1862,7 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
         return KAT_ERR_WORKSPACE;
       if (allow_dynamic_smem(dev, bwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
         return KAT_ERR_CUDA;
+      p.num_stride = num_stride;
       if (launch_bwd_tma(dtype, x, grad_out, grad_x, numerator, denominator,
                          static_cast<double*>(workspace), p, q, s) != cudaSuccess)
         return KAT_ERR_CUDA;
@@ -1827,6 +1876,7 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
                          dtype, vec, &p);
   }
   if (st != KAT_OK) return st;
+  p.num_stride = num_stride;
   if (p.blocks > 0) {
     if (workspace == nullptr || workspace_bytes < p.workspace_bytes ||
         (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
@@ -1969,6 +2019,8 @@ int fwd_impl(const void* x, void* y, const float* numerator, const float* denomi
   int64_t n = 0;
   int st = validate_dims(batch, channels, inner, num_groups, dtype, &n);
   if (st != KAT_OK) return st;
+  const int num_stride = (formula & KAT_SHARED_NUMERATOR) ? 0 : 6;
+  formula &= ~KAT_SHARED_NUMERATOR;
   if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
   if (numerator == nullptr || denominator == nullptr) return KAT_ERR_NULL_POINTER;
   if (n == 0) return KAT_OK;
@@ -1985,6 +2037,7 @@ int fwd_impl(const void* x, void* y, const float* numerator, const float* denomi
       if (st != KAT_OK) return st;
       if (allow_dynamic_smem(dev, fwd_tma_kernel_for(dtype), q.smem_bytes) != cudaSuccess)
         return KAT_ERR_CUDA;
+      p.num_stride = num_stride;
       if (launch_fwd_tma(dtype, x, y, numerator, denominator, p, q,
                          static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return KAT_ERR_CUDA;
@@ -1994,6 +2047,7 @@ int fwd_impl(const void* x, void* y, const float* numerator, const float* denomi
   st = plan_for_launch(fwd_kernel_for(dtype, vec, formula), batch, channels, inner, num_groups,
                        dtype, vec, &p);
   if (st != KAT_OK) return st;
+  p.num_stride = num_stride;
   if (launch_fwd(dtype, vec, formula, x, y, numerator, denominator, p,
                  static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return KAT_ERR_CUDA;

@@ -46,13 +46,18 @@ def _check_cuda(name: str, t: Tensor) -> None:
                            f"the CUDA path has no CPU implementation")
 
 
-def _check_counts(n: Tensor, d: Tensor, group: int) -> None:
-    assert n.numel() == group * 6, f"numerator: expected {group*6} coeffs, got {n.numel()}"
+def _shared(formula: int) -> bool:
+    return bool(formula & _native.KAT_SHARED_NUMERATOR)
+
+
+def _check_counts(n: Tensor, d: Tensor, group: int, shared: bool = False) -> None:
+    n_rows = 1 if shared else group
+    assert n.numel() == n_rows * 6, f"numerator: expected {n_rows*6} coeffs, got {n.numel()}"
     assert d.numel() == group * 4, f"denominator: expected {group*4} coeffs, got {d.numel()}"
 
 
-def _coefficients(n: Tensor, d: Tensor, group: int, device: torch.device):
-    _check_counts(n, d, group)
+def _coefficients(n: Tensor, d: Tensor, group: int, device: torch.device, shared: bool = False):
+    _check_counts(n, d, group, shared)
     n32 = n.detach().to(device=device, dtype=torch.float32).contiguous()
     d32 = d.detach().to(device=device, dtype=torch.float32).contiguous()
     return n32, d32
@@ -111,13 +116,16 @@ def _fwd_f64(x: Tensor, n: Tensor, d: Tensor, group: int, dims, formula: int) ->
 
 def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims,
          formula: int = _native.KAT_FORMULA_KAT) -> Tensor:
-    _check_counts(n, d, group)
+    shared = _shared(formula)
+    _check_counts(n, d, group, shared)
     _check_cuda("input", x)
     if x.dtype == torch.float64:
+        if shared:
+            n, formula = n.reshape(1, 6).expand(group, 6), formula & ~_native.KAT_SHARED_NUMERATOR
         return _fwd_f64(x, n, d, group, dims, formula)
     code = _dtype_code(x)
     x = x.contiguous()
-    n32, d32 = _coefficients(n, d, group, x.device)
+    n32, d32 = _coefficients(n, d, group, x.device, shared)
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
     with torch.cuda.device(x.device):
         args = (x.data_ptr(), y.data_ptr(), n32.data_ptr(), d32.data_ptr(),
@@ -133,7 +141,8 @@ def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims,
 
 def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
          need_dx: bool = True, exchange=None, formula: int = _native.KAT_FORMULA_KAT):
-    _check_counts(n, d, group)
+    shared = _shared(formula)
+    _check_counts(n, d, group, shared)
     _check_cuda("input", x)
     _check_cuda("grad_output", grad_output)
     if x.dtype == torch.float64:
@@ -150,7 +159,7 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
     if grad_output.shape != x.shape:
         raise ValueError(f"kat_rational: grad_output shape {tuple(grad_output.shape)} != "
                          f"input shape {tuple(x.shape)}")
-    n32, d32 = _coefficients(n, d, group, x.device)
+    n32, d32 = _coefficients(n, d, group, x.device, shared)
     d_x = torch.empty_like(x, memory_format=torch.contiguous_format) if need_dx else None
     d_n = torch.empty(n.shape, dtype=torch.float32, device=x.device)
     d_d = torch.empty(d.shape, dtype=torch.float32, device=x.device)
@@ -291,6 +300,41 @@ class RationalCUDA2DDP(torch.autograd.Function):
         d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
                                      ctx.group, _dims_2d(input, ctx.group),
                                      need_dx=ctx.needs_input_grad[0], exchange=ctx.exchange)
+        return d_input, d_num, d_den, None, None
+
+
+_KAT_SHARED = _native.KAT_FORMULA_KAT | _native.KAT_SHARED_NUMERATOR
+
+
+class KatGroupFunction(torch.autograd.Function):
+    """The Function KAT_Group / KAT_Group2D apply on the CUDA kernels: the module's
+    weight_numerator [1, 6] reaches the kernels as one row shared by every group
+    (KAT_SHARED_NUMERATOR), so the reference's per-forward repeat to [G, 6]
+    (kat_rational/kat_1dgroup_triton.py:86) and its backward (a sum over groups) do not run as
+    separate launches: the grid reduction writes d_numerator [1, 6] summed over groups in a
+    fixed fp64 order.  Values and d_input, d_denominator equal RationalCUDA1DGroup /
+    RationalCUDA2D on the repeated numerator bit for bit.  `nchw` selects the [B, C, H, W]
+    layout."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
+    def forward(ctx, input: Tensor, weight_numerator: Tensor, weight_denominator: Tensor,
+                group: int, nchw: bool = False) -> Tensor:
+        ctx.save_for_backward(input, weight_numerator, weight_denominator)
+        ctx.group = group
+        ctx.nchw = nchw
+        dims = _dims_2d(input, group) if nchw else _dims_1d(input, group)
+        return _fwd(input, weight_numerator, weight_denominator, group, dims, _KAT_SHARED)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output: Tensor):
+        input, weight_numerator, weight_denominator = ctx.saved_tensors
+        group = ctx.group
+        dims = _dims_2d(input, group) if ctx.nchw else _dims_1d(input, group)
+        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
+                                     group, dims, need_dx=ctx.needs_input_grad[0],
+                                     formula=_KAT_SHARED)
         return d_input, d_num, d_den, None, None
 
 
