@@ -17,11 +17,21 @@ by the sm_100a kernels in libkat_rational.so; nothing here computes on the CPU.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 from torch import Tensor
 
 from . import _native
+
+# KAT_RATIONAL_NVTX=1: every forward / backward call of the library is wrapped in an NVTX range
+# ("kat_rational.fwd [shape] dtype" / "kat_rational.bwd ..."), so profiler timelines and ncu
+# --nvtx filters can attribute kernels to module calls.  Off by default (no per-call cost).
+_NVTX = os.environ.get("KAT_RATIONAL_NVTX", "") == "1"
+
+
+def _nvtx_push(kind: str, x: Tensor) -> None:
+    torch.cuda.nvtx.range_push(f"kat_rational.{kind} {list(x.shape)} {str(x.dtype)[6:]}")
 
 _DTYPE_CODES = {
     torch.float32: _native.KAT_DTYPE_F32,
@@ -127,6 +137,8 @@ def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims,
     x = x.contiguous()
     n32, d32 = _coefficients(n, d, group, x.device, shared)
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    if _NVTX:
+        _nvtx_push("fwd", x)
     with torch.cuda.device(x.device):
         args = (x.data_ptr(), y.data_ptr(), n32.data_ptr(), d32.data_ptr(),
                 dims[0], dims[1], dims[2], group, code)
@@ -135,6 +147,8 @@ def _fwd(x: Tensor, n: Tensor, d: Tensor, group: int, dims,
         else:
             status = _native.lib().kat_rational_fwd_formula(*args, formula,
                                                             _stream_ptr(x.device))
+    if _NVTX:
+        torch.cuda.nvtx.range_pop()
     _native.check("kat_rational_fwd", status)
     return y
 
@@ -163,6 +177,10 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
     d_x = torch.empty_like(x, memory_format=torch.contiguous_format) if need_dx else None
     d_n = torch.empty(n.shape, dtype=torch.float32, device=x.device)
     d_d = torch.empty(d.shape, dtype=torch.float32, device=x.device)
+    if exchange is not None and formula != _native.KAT_FORMULA_KAT:
+        raise ValueError("kat_rational: the fused exchange computes the KAT formula only")
+    if _NVTX:
+        _nvtx_push("bwd", x)
     with torch.cuda.device(x.device):
         ws_bytes = _workspace_bytes(dims, group, code, x.device)
         ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
@@ -170,8 +188,6 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
                 d_x.data_ptr() if d_x is not None else None, n32.data_ptr(), d32.data_ptr(),
                 d_n.data_ptr(), d_d.data_ptr(), ws.data_ptr(), ws.numel(), dims[0], dims[1],
                 dims[2], group, code)
-        if exchange is not None and formula != _native.KAT_FORMULA_KAT:
-            raise ValueError("kat_rational: the fused exchange computes the KAT formula only")
         if exchange is None and formula != _native.KAT_FORMULA_KAT:
             status = _native.lib().kat_rational_bwd_formula(*args, formula,
                                                             _stream_ptr(x.device))
@@ -180,6 +196,8 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
         else:
             status = _native.lib().kat_rational_bwd_allreduce(
                 *args, ctypes.byref(exchange.peers), _stream_ptr(x.device))
+    if _NVTX:
+        torch.cuda.nvtx.range_pop()
     _native.check("kat_rational_bwd", status)
     return d_x, d_n, d_d
 
