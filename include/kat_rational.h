@@ -70,8 +70,8 @@ extern "C" {
  * which the reference repeats per group on every forward: kat_rational/kat_1dgroup_triton.py:86),
  * and the backward writes grad_numerator as ONE row [6], the sum over groups of the per-group
  * gradients (added in fp64 in a fixed order, rounded once) — the gradient the reference's
- * repeat backward produces, without the repeat and the sum as separate launches.  Not accepted
- * by the data-parallel entry points. */
+ * repeat backward produces, without the repeat and the sum as separate launches.  Also accepted
+ * by kat_rational_bwd_allreduce_formula (data parallel). */
 #define KAT_SHARED_NUMERATOR 0x100
 
 /*
@@ -258,6 +258,21 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
                                int64_t batch, int64_t channels, int64_t inner,
                                int64_t num_groups, int dtype,
                                const kat_rational_peers* peers, void* stream);
+
+/*
+ * kat_rational_bwd_allreduce with a `formula` argument: KAT_FORMULA_KAT, optionally or-ed with
+ * KAT_SHARED_NUMERATOR (one numerator row [6] for every group; grad_numerator [6] is the sum
+ * over groups of the rank-summed per-group gradients, added in the same fixed fp64 order as
+ * kat_rational_bwd_formula's, so at world size 1 both give the same bits).  The abs-after-sum
+ * formula is refused (KAT_ERR_BAD_FORMULA).  No counterpart in the reference.
+ */
+int kat_rational_bwd_allreduce_formula(const void* x, const void* grad_out, void* grad_x,
+                                       const float* numerator, const float* denominator,
+                                       float* grad_numerator, float* grad_denominator,
+                                       void* workspace, size_t workspace_bytes,
+                                       int64_t batch, int64_t channels, int64_t inner,
+                                       int64_t num_groups, int dtype, int formula,
+                                       const kat_rational_peers* peers, void* stream);
 
 /*
  * The exchange step alone, for callers that reduce their coefficient gradients themselves (the

@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "kat_rational_exchange_buffer_bytes",
     "kat_rational_bwd_allreduce",
     "kat_rational_exchange_grads",
+    "kat_rational_bwd_allreduce_formula",
     "kat_rational_enable_peer_access",
     "kat_rational_exchange_create",
     "kat_rational_exchange_open",
@@ -185,6 +186,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.kat_rational_exchange_open.restype = i32
     lib.kat_rational_exchange_close.argtypes = [vp]
     lib.kat_rational_exchange_close.restype = i32
+    lib.kat_rational_bwd_allreduce_formula.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp,
+                                                       ctypes.c_size_t, i64, i64, i64, i64, i32,
+                                                       i32, vp, vp]
+    lib.kat_rational_bwd_allreduce_formula.restype = i32
     lib.kat_rational_exchange_grads.argtypes = [vp, vp, i64, vp, vp]
     lib.kat_rational_exchange_grads.restype = i32
     lib.kat_rational_exchange_destroy.argtypes = [vp]

@@ -1098,11 +1098,22 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   __syncthreads();
   const bool ok = exchange_rows(s_sum, G * kAcc, peers);
   const double scale = peers.average ? 1.0 / double(peers.world) : 1.0;
+  const bool shared = p.num_stride == 0;   // one numerator row: its gradient summed over groups
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
 #pragma unroll
     for (int k = 0; k < kAcc; ++k) tot[k] = s_sum[g * kAcc + k];
-    write_group(tot, scale, ok, g, lane, den, dnum, dden, p.formula);
+    if (!shared || lane >= 6) write_group(tot, scale, ok, g, lane, den, dnum, dden, p.formula);
+  }
+  if (shared && tid < 6) {
+    // the order of kat_bwd_reduce_shared_kernel: groups w, w + 8, ... per warp w, then warps
+    double v = 0.0;
+    for (int w = 0; w < kReduceWarps; ++w) {
+      double a = 0.0;
+      for (int g = w; g < G; g += kReduceWarps) a += s_sum[g * kAcc + tid];
+      v += a;
+    }
+    dnum[tid] = ok ? float(v * scale) : __int_as_float(0x7fc00000);
   }
 }
 
@@ -1821,7 +1832,7 @@ int bwd_impl(const void* x, const void* grad_out, void* grad_x, const float* num
   const bool shared = (formula & KAT_SHARED_NUMERATOR) != 0;
   formula &= ~KAT_SHARED_NUMERATOR;
   if (formula != kFormulaKat && formula != kFormulaAbsSum) return KAT_ERR_BAD_FORMULA;
-  if (shared && peers != nullptr) return KAT_ERR_BAD_FORMULA;
+  if (peers != nullptr && formula != kFormulaKat) return KAT_ERR_BAD_FORMULA;
   const int num_stride = shared ? 0 : 6;
   if (numerator == nullptr || denominator == nullptr || grad_numerator == nullptr ||
       grad_denominator == nullptr)
@@ -2260,6 +2271,22 @@ int kat_rational_bwd_allreduce(const void* x, const void* grad_out, void* grad_x
   return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
                   workspace, workspace_bytes, batch, channels, inner, num_groups, dtype,
                   kFormulaKat, stream, &pe);
+}
+
+int kat_rational_bwd_allreduce_formula(const void* x, const void* grad_out, void* grad_x,
+                                       const float* numerator, const float* denominator,
+                                       float* grad_numerator, float* grad_denominator,
+                                       void* workspace, size_t workspace_bytes, int64_t batch,
+                                       int64_t channels, int64_t inner, int64_t num_groups,
+                                       int dtype, int formula, const kat_rational_peers* peers,
+                                       void* stream) {
+  if ((formula & ~KAT_SHARED_NUMERATOR) != kFormulaKat) return KAT_ERR_BAD_FORMULA;
+  Peers pe;
+  const int st = peers_from(peers, num_groups, &pe);
+  if (st != KAT_OK) return st;
+  return bwd_impl(x, grad_out, grad_x, numerator, denominator, grad_numerator, grad_denominator,
+                  workspace, workspace_bytes, batch, channels, inner, num_groups, dtype,
+                  formula, stream, &pe);
 }
 
 int kat_rational_exchange_grads(float* grad_numerator, float* grad_denominator,

@@ -19,7 +19,7 @@ import torch.nn as nn
 
 from ._init_table import INIT_JSON
 from .kat_1dgroup_torch import Rational_CUDA_A_1DGroup
-from .rational_cuda import KatGroupFunction, RationalCUDA1DGroup, RationalCUDA1DGroupDP
+from .rational_cuda import KatGroupFunction, RationalCUDA1DGroup
 
 
 class KAT_Group(nn.Module):
@@ -65,9 +65,8 @@ class KAT_Group(nn.Module):
         assert input.dim() == 3 or input.dim() == 2, \
             "Input tensor must be 3D (batch, length, channels) or 2D (batch, channels)."
         if getattr(self, "exchange", None) is not None:
-            weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
-            return RationalCUDA1DGroupDP.apply(input, weight_numerator, self.weight_denominator,
-                                               self.num_groups, self.exchange)
+            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
+                                          self.num_groups, False, self.exchange)
         if self.rational == RationalCUDA1DGroup.apply:
             # the shared numerator row goes to the kernels as is (no repeat / sum launches)
             return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,

@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from ._init_table import INIT_JSON
-from .rational_cuda import KatGroupFunction, RationalCUDA2D, RationalCUDA2DDP
+from .rational_cuda import KatGroupFunction, RationalCUDA2D
 
 
 class KAT_Group2D(nn.Module):
@@ -51,9 +51,8 @@ class KAT_Group2D(nn.Module):
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         assert input.dim() == 4, "Input tensor must be 4D (batch, channels, height, width)."
         if getattr(self, "exchange", None) is not None:
-            weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
-            return RationalCUDA2DDP.apply(input, weight_numerator, self.weight_denominator,
-                                          self.num_groups, self.exchange)
+            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
+                                          self.num_groups, True, self.exchange)
         if self.rational == RationalCUDA2D.apply:
             # the shared numerator row goes to the kernels as is (no repeat / sum launches)
             return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,

@@ -177,7 +177,7 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
     d_x = torch.empty_like(x, memory_format=torch.contiguous_format) if need_dx else None
     d_n = torch.empty(n.shape, dtype=torch.float32, device=x.device)
     d_d = torch.empty(d.shape, dtype=torch.float32, device=x.device)
-    if exchange is not None and formula != _native.KAT_FORMULA_KAT:
+    if exchange is not None and (formula & ~_native.KAT_SHARED_NUMERATOR) != _native.KAT_FORMULA_KAT:
         raise ValueError("kat_rational: the fused exchange computes the KAT formula only")
     if _NVTX:
         _nvtx_push("bwd", x)
@@ -193,9 +193,12 @@ def _bwd(grad_output: Tensor, x: Tensor, n: Tensor, d: Tensor, group: int, dims,
                                                             _stream_ptr(x.device))
         elif exchange is None:
             status = _native.lib().kat_rational_bwd(*args, _stream_ptr(x.device))
-        else:
+        elif formula == _native.KAT_FORMULA_KAT:
             status = _native.lib().kat_rational_bwd_allreduce(
                 *args, ctypes.byref(exchange.peers), _stream_ptr(x.device))
+        else:
+            status = _native.lib().kat_rational_bwd_allreduce_formula(
+                *args, formula, ctypes.byref(exchange.peers), _stream_ptr(x.device))
     if _NVTX:
         torch.cuda.nvtx.range_pop()
     _native.check("kat_rational_bwd", status)
@@ -278,49 +281,6 @@ class RationalCUDA2D(torch.autograd.Function):
         return d_input, d_num, d_den, None
 
 
-class RationalCUDA1DGroupDP(torch.autograd.Function):
-    """RationalCUDA1DGroup whose backward also exchanges the coefficient gradients with the
-    other ranks of `exchange` (a distributed.PeerExchange) inside the reduction kernel."""
-
-    @staticmethod
-    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
-    def forward(ctx, input, weight_numerator, weight_denominator, group, exchange):
-        ctx.save_for_backward(input, weight_numerator, weight_denominator)
-        ctx.group = group
-        ctx.exchange = exchange
-        return rational_fwd_cuda(input, weight_numerator, weight_denominator, group)
-
-    @staticmethod
-    @torch.amp.custom_bwd(device_type="cuda")
-    def backward(ctx, grad_output):
-        input, weight_numerator, weight_denominator = ctx.saved_tensors
-        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
-                                     ctx.group, _dims_1d(input, ctx.group),
-                                     need_dx=ctx.needs_input_grad[0], exchange=ctx.exchange)
-        return d_input, d_num, d_den, None, None
-
-
-class RationalCUDA2DDP(torch.autograd.Function):
-    """RationalCUDA2D with the cross-rank coefficient-gradient exchange in its backward."""
-
-    @staticmethod
-    @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
-    def forward(ctx, input, weight_numerator, weight_denominator, group, exchange):
-        ctx.save_for_backward(input, weight_numerator, weight_denominator)
-        ctx.group = group
-        ctx.exchange = exchange
-        return rational_fwd_cuda_2d(input, weight_numerator, weight_denominator, group)
-
-    @staticmethod
-    @torch.amp.custom_bwd(device_type="cuda")
-    def backward(ctx, grad_output):
-        input, weight_numerator, weight_denominator = ctx.saved_tensors
-        d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
-                                     ctx.group, _dims_2d(input, ctx.group),
-                                     need_dx=ctx.needs_input_grad[0], exchange=ctx.exchange)
-        return d_input, d_num, d_den, None, None
-
-
 _KAT_SHARED = _native.KAT_FORMULA_KAT | _native.KAT_SHARED_NUMERATOR
 
 
@@ -332,15 +292,18 @@ class KatGroupFunction(torch.autograd.Function):
     separate launches: the grid reduction writes d_numerator [1, 6] summed over groups in a
     fixed fp64 order.  Values and d_input, d_denominator equal RationalCUDA1DGroup /
     RationalCUDA2D on the repeated numerator bit for bit.  `nchw` selects the [B, C, H, W]
-    layout."""
+    layout; with `exchange` (a distributed.PeerExchange) the backward also exchanges the
+    coefficient gradients with the other ranks (kat_rational_bwd_allreduce_formula), summing the
+    numerator over groups in the same order as the local backward."""
 
     @staticmethod
     @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
     def forward(ctx, input: Tensor, weight_numerator: Tensor, weight_denominator: Tensor,
-                group: int, nchw: bool = False) -> Tensor:
+                group: int, nchw: bool = False, exchange=None) -> Tensor:
         ctx.save_for_backward(input, weight_numerator, weight_denominator)
         ctx.group = group
         ctx.nchw = nchw
+        ctx.exchange = exchange
         dims = _dims_2d(input, group) if nchw else _dims_1d(input, group)
         return _fwd(input, weight_numerator, weight_denominator, group, dims, _KAT_SHARED)
 
@@ -352,8 +315,8 @@ class KatGroupFunction(torch.autograd.Function):
         dims = _dims_2d(input, group) if ctx.nchw else _dims_1d(input, group)
         d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
                                      group, dims, need_dx=ctx.needs_input_grad[0],
-                                     formula=_KAT_SHARED)
-        return d_input, d_num, d_den, None, None
+                                     exchange=ctx.exchange, formula=_KAT_SHARED)
+        return d_input, d_num, d_den, None, None, None
 
 
 # The reference's export names (kat_rational/__init__.py:2, rational_triton2d.py:226).
