@@ -84,6 +84,8 @@ def parse_args():
     ap.add_argument("--gpu-bar-child", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--sweep", action="store_true",
                     help="print one line per bandwidth-sweep point (kernel timings) instead")
+    ap.add_argument("--sweep-logn", default="",
+                    help="with --sweep: only the points with these log2(elements), e.g. 20,24")
     ap.add_argument("--vit-batch", type=int, default=128,
                     help="per-GPU batch of the GR-KAN ViT-B/16 training step (--workload "
                          "grkan_vit_b16)")
@@ -897,7 +899,10 @@ def run_sweep(args):
     peak, peak_kind = measured_peak()
     stream = torch.cuda.current_stream(dev)
     sp = ctypes.c_void_p(stream.cuda_stream)
+    keep = {int(v) for v in args.sweep_logn.split(",") if v.strip()}
     for c, g, n, dt in workloads.sweep_points():
+        if keep and n.bit_length() - 1 not in keep:
+            continue
         w = workloads.sweep(c, g, n, dt)
         N = w.numel
         eb = {"f32": 4, "bf16": 2, "f16": 2}[dt]
