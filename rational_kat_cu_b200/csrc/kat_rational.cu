@@ -490,30 +490,68 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
 
 // Sum of group g's 10 coefficient slots over all blocks of the grid, computed by one warp:
 // lane j takes blocks j, j+32, ... in order (each block's segments in order), then the 10
-// lane totals are added with a fixed xor tree, leaving the result in every lane.
+// lane totals are added with a fixed xor tree, leaving the result in every lane.  The segments
+// of a block that hold group g are the column blocks cb0 .. cb1 of the block's item range that
+// meet the group's vector columns; the loads of four consecutive blocks of a lane are issued
+// before any of them is added, so a lane waits for memory once per four blocks (the order of
+// the additions is the block order all the same).
+__device__ __forceinline__ const double* group_slot(const double* __restrict__ partial,
+                                                    const Plan& p, int64_t blk, int64_t seg,
+                                                    int64_t lg) {
+  const double* src = partial + ((blk * p.max_segments + seg) * p.max_local_groups + lg) * kAcc;
+  if (!kat_check(seg < p.max_segments && lg < p.max_local_groups) ||
+      !in_bounds(partial, int64_t(p.workspace_bytes / sizeof(double)), src, kAcc))
+    return nullptr;
+  return src;
+}
+
 __device__ __forceinline__ void group_totals(const double* __restrict__ partial, const Plan& p,
                                              int64_t g, int lane, double (&tot)[kAcc]) {
 #pragma unroll
   for (int k = 0; k < kAcc; ++k) tot[k] = 0.0;
-  for (int64_t blk = lane; blk < p.blocks; blk += 32) {
-    int64_t i0, i1;
-    block_items(p, blk, i0, i1);
-    const int64_t cb0 = fast_div(i0, p.rows_m, p.rows_s1, p.rows_s2);
-    const int64_t cb1 = fast_div(i1 - 1, p.rows_m, p.rows_s1, p.rows_s2);
-    for (int64_t cb = cb0; cb <= cb1; ++cb) {
-      const int64_t col0 = cb * p.tile_cols;
-      const int64_t col_end = min(col0 + p.tile_cols, p.vec_cols);
-      const int64_t g_first = fast_div(col0, p.vg_m, p.vg_s1, p.vg_s2);
-      const int64_t g_last = fast_div(col_end - 1, p.vg_m, p.vg_s1, p.vg_s2);
-      if (g < g_first) break;
-      if (g > g_last) continue;
-      const double* src =
-          partial + ((blk * p.max_segments + (cb - cb0)) * p.max_local_groups + (g - g_first)) * kAcc;
-      if (!kat_check(cb - cb0 < p.max_segments && g - g_first < p.max_local_groups) ||
-          !in_bounds(partial, int64_t(p.workspace_bytes / sizeof(double)), src, kAcc))
-        continue;
+  // column blocks that meet group g's vector columns [g vg, (g + 1) vg)
+  const int64_t cb_lo = (g * p.vec_group) / p.tile_cols;
+  const int64_t cb_hi = ((g + 1) * p.vec_group - 1) / p.tile_cols;
+  constexpr int kAhead = 4;
+  for (int64_t b0 = lane; b0 < p.blocks; b0 += 32 * kAhead) {
+    int64_t lo[kAhead], hi[kAhead], c0[kAhead];
+    const double* first[kAhead];
+    double v[kAhead][kAcc];
 #pragma unroll
-      for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
+    for (int a = 0; a < kAhead; ++a) {
+      const int64_t blk = b0 + 32 * a;
+      first[a] = nullptr;
+      lo[a] = 1;
+      hi[a] = 0;
+      c0[a] = 0;
+      if (blk < p.blocks) {
+        int64_t i0, i1;
+        block_items(p, blk, i0, i1);
+        c0[a] = fast_div(i0, p.rows_m, p.rows_s1, p.rows_s2);
+        const int64_t c1 = fast_div(i1 - 1, p.rows_m, p.rows_s1, p.rows_s2);
+        lo[a] = max(c0[a], cb_lo);
+        hi[a] = min(c1, cb_hi);
+        if (lo[a] <= hi[a]) {
+          const int64_t gf = fast_div(lo[a] * p.tile_cols, p.vg_m, p.vg_s1, p.vg_s2);
+          first[a] = group_slot(partial, p, blk, lo[a] - c0[a], g - gf);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kAcc; ++k) v[a][k] = first[a] != nullptr ? first[a][k] : 0.0;
+    }
+#pragma unroll
+    for (int a = 0; a < kAhead; ++a) {
+      if (first[a] == nullptr) continue;
+#pragma unroll
+      for (int k = 0; k < kAcc; ++k) tot[k] += v[a][k];
+      // further column blocks of this block that hold part of the group (wide groups)
+      for (int64_t cb = lo[a] + 1; cb <= hi[a]; ++cb) {
+        const int64_t gf = fast_div(cb * p.tile_cols, p.vg_m, p.vg_s1, p.vg_s2);
+        const double* src = group_slot(partial, p, b0 + 32 * a, cb - c0[a], g - gf);
+        if (src == nullptr) continue;
+#pragma unroll
+        for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
+      }
     }
   }
 #pragma unroll

@@ -19,7 +19,7 @@ import torch.nn as nn
 
 from ._init_table import INIT_JSON
 from .kat_1dgroup_torch import Rational_CUDA_A_1DGroup
-from .rational_cuda import KatGroupFunction, RationalCUDA1DGroup
+from .rational_cuda import SHARED_ROW_MAX_GROUPS, KatGroupFunction, RationalCUDA1DGroup
 
 
 class KAT_Group(nn.Module):
@@ -64,13 +64,15 @@ class KAT_Group(nn.Module):
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         assert input.dim() == 3 or input.dim() == 2, \
             "Input tensor must be 3D (batch, length, channels) or 2D (batch, channels)."
-        if getattr(self, "exchange", None) is not None:
-            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
-                                          self.num_groups, False, self.exchange)
-        if self.rational == RationalCUDA1DGroup.apply:
-            # the shared numerator row goes to the kernels as is (no repeat / sum launches)
-            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
-                                          self.num_groups, False)
+        exchange = getattr(self, "exchange", None)
+        if exchange is not None or self.rational == RationalCUDA1DGroup.apply:
+            # up to SHARED_ROW_MAX_GROUPS groups the numerator row goes to the kernels as is
+            # (no repeat / sum launches); the same choice with and without the exchange
+            shared = self.num_groups <= SHARED_ROW_MAX_GROUPS
+            num = (self.weight_numerator if shared
+                   else self.weight_numerator.repeat(self.num_groups, 1))
+            return KatGroupFunction.apply(input, num, self.weight_denominator, self.num_groups,
+                                          False, exchange, shared)
         weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
         if self.rational is Rational_CUDA_A_1DGroup and input.dim() == 2:
             return self.rational(input.unsqueeze(0), weight_numerator, self.weight_denominator,

@@ -13,7 +13,7 @@ import torch
 import torch.nn as nn
 
 from ._init_table import INIT_JSON
-from .rational_cuda import KatGroupFunction, RationalCUDA2D
+from .rational_cuda import SHARED_ROW_MAX_GROUPS, KatGroupFunction, RationalCUDA2D
 
 
 class KAT_Group2D(nn.Module):
@@ -50,13 +50,15 @@ class KAT_Group2D(nn.Module):
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         assert input.dim() == 4, "Input tensor must be 4D (batch, channels, height, width)."
-        if getattr(self, "exchange", None) is not None:
-            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
-                                          self.num_groups, True, self.exchange)
-        if self.rational == RationalCUDA2D.apply:
-            # the shared numerator row goes to the kernels as is (no repeat / sum launches)
-            return KatGroupFunction.apply(input, self.weight_numerator, self.weight_denominator,
-                                          self.num_groups, True)
+        exchange = getattr(self, "exchange", None)
+        if exchange is not None or self.rational == RationalCUDA2D.apply:
+            # up to SHARED_ROW_MAX_GROUPS groups the numerator row goes to the kernels as is
+            # (no repeat / sum launches); the same choice with and without the exchange
+            shared = self.num_groups <= SHARED_ROW_MAX_GROUPS
+            num = (self.weight_numerator if shared
+                   else self.weight_numerator.repeat(self.num_groups, 1))
+            return KatGroupFunction.apply(input, num, self.weight_denominator, self.num_groups,
+                                          True, exchange, shared)
         weight_numerator = self.weight_numerator.repeat(self.num_groups, 1)
         return self.rational(input, weight_numerator, self.weight_denominator, self.num_groups)
 

@@ -283,6 +283,11 @@ class RationalCUDA2D(torch.autograd.Function):
 
 _KAT_SHARED = _native.KAT_FORMULA_KAT | _native.KAT_SHARED_NUMERATOR
 
+# The shared-row grid reduction runs in one block of 8 warps, each summing its groups one after
+# the other: up to 16 groups (two per warp) it costs no more than the per-group reduction; above
+# that the modules repeat the numerator per group and let torch sum its gradient instead.
+SHARED_ROW_MAX_GROUPS = 16
+
 
 class KatGroupFunction(torch.autograd.Function):
     """The Function KAT_Group / KAT_Group2D apply on the CUDA kernels: the module's
@@ -294,18 +299,20 @@ class KatGroupFunction(torch.autograd.Function):
     RationalCUDA2D on the repeated numerator bit for bit.  `nchw` selects the [B, C, H, W]
     layout; with `exchange` (a distributed.PeerExchange) the backward also exchanges the
     coefficient gradients with the other ranks (kat_rational_bwd_allreduce_formula), summing the
-    numerator over groups in the same order as the local backward."""
+    numerator over groups in the same order as the local backward.  shared=False takes the
+    reference's contract instead (numerator [G, 6], d_numerator [G, 6])."""
 
     @staticmethod
     @torch.amp.custom_fwd(cast_inputs=torch.float32, device_type="cuda")
     def forward(ctx, input: Tensor, weight_numerator: Tensor, weight_denominator: Tensor,
-                group: int, nchw: bool = False, exchange=None) -> Tensor:
+                group: int, nchw: bool = False, exchange=None, shared: bool = True) -> Tensor:
         ctx.save_for_backward(input, weight_numerator, weight_denominator)
         ctx.group = group
         ctx.nchw = nchw
         ctx.exchange = exchange
+        ctx.formula = _KAT_SHARED if shared else _native.KAT_FORMULA_KAT
         dims = _dims_2d(input, group) if nchw else _dims_1d(input, group)
-        return _fwd(input, weight_numerator, weight_denominator, group, dims, _KAT_SHARED)
+        return _fwd(input, weight_numerator, weight_denominator, group, dims, ctx.formula)
 
     @staticmethod
     @torch.amp.custom_bwd(device_type="cuda")
@@ -315,8 +322,8 @@ class KatGroupFunction(torch.autograd.Function):
         dims = _dims_2d(input, group) if ctx.nchw else _dims_1d(input, group)
         d_input, d_num, d_den = _bwd(grad_output, input, weight_numerator, weight_denominator,
                                      group, dims, need_dx=ctx.needs_input_grad[0],
-                                     exchange=ctx.exchange, formula=_KAT_SHARED)
-        return d_input, d_num, d_den, None, None, None
+                                     exchange=ctx.exchange, formula=ctx.formula)
+        return d_input, d_num, d_den, None, None, None, None
 
 
 # The reference's export names (kat_rational/__init__.py:2, rational_triton2d.py:226).

@@ -71,3 +71,27 @@ def test_modules_take_the_shared_row_path():
     m2 = kat.KAT_Group2D(num_groups=8, mode="identity").cuda()
     y2 = m2(torch.randn(2, 16, 3, 3, device="cuda"))
     assert type(y2.grad_fn).__name__.startswith("KatGroupFunction")
+
+
+def test_many_groups_take_the_per_group_path():
+    """Above SHARED_ROW_MAX_GROUPS groups the modules repeat the numerator (the per-group grid
+    reduction is faster there): results and gradients are those of RationalCUDA1DGroup on the
+    repeated numerator, bit for bit."""
+    from rational_kat_cu_b200.rational_cuda import SHARED_ROW_MAX_GROUPS
+
+    G = 64
+    assert G > SHARED_ROW_MAX_GROUPS
+    m = kat.KAT_Group(num_groups=G, mode="gelu").cuda()
+    g = torch.Generator(device="cpu").manual_seed(9)
+    x = torch.randn(16, 768, generator=g).to(torch.bfloat16).cuda().requires_grad_(True)
+    gy = torch.randn(16, 768, generator=g).to(torch.bfloat16).cuda()
+    y = m(x)
+    y.backward(gy)
+    xr = x.detach().clone().requires_grad_(True)
+    n = m.weight_numerator.detach().clone().requires_grad_(True)
+    d = m.weight_denominator.detach().clone().requires_grad_(True)
+    yr = RationalCUDA1DGroup.apply(xr, n.repeat(G, 1), d, G)
+    yr.backward(gy)
+    assert torch.equal(y, yr) and torch.equal(x.grad, xr.grad)
+    assert torch.equal(m.weight_numerator.grad, n.grad)
+    assert torch.equal(m.weight_denominator.grad, d.grad)
