@@ -67,7 +67,7 @@ def parse_args():
     ap.add_argument("--workload", default="kat_group_vitb_bf16")
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of a CUDA graph")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--e2e-chunks", type=int, default=16,
+    ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="row chunks the host-buffer pipeline overlaps")
     ap.add_argument("--kernel-iters", type=int, default=100)
     ap.add_argument("--cpu-seconds", type=float, default=30.0,

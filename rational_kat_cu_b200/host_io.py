@@ -39,7 +39,7 @@ class HostPipeline:
     formula) over pinned host tensors with overlapped copies.  Device buffers are kept for
     reuse while the input shape stays."""
 
-    def __init__(self, module: torch.nn.Module, chunks: int = 16, slots: int = 3,
+    def __init__(self, module: torch.nn.Module, chunks: int = 4, slots: int = 3,
                  device: Optional[torch.device] = None):
         self.module = module
         self.chunks = chunks
