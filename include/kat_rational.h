@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define KAT_RATIONAL_ABI_VERSION 2
+#define KAT_RATIONAL_ABI_VERSION 3
 
 /* Data-tensor element types. */
 #define KAT_DTYPE_F32 0
@@ -317,6 +317,11 @@ typedef struct kat_rational_plan {
   int32_t max_segments;  /* column blocks one block can touch */
   int32_t max_local_groups;  /* groups one column block can touch */
   uint64_t workspace_bytes;  /* backward partial-sum buffer */
+  /* Block split: 0 = the items are split evenly over all blocks; > 0 = each block stays in
+   * one column block, the first `col_block_extra` column blocks get col_block_blocks + 1
+   * blocks and the others col_block_blocks, and a column block's rows are split evenly. */
+  int64_t col_block_blocks;
+  int64_t col_block_extra;
 } kat_rational_plan;
 
 int kat_rational_make_plan(int64_t batch, int64_t channels, int64_t inner,

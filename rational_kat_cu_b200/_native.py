@@ -79,7 +79,7 @@ class KatPeers(ctypes.Structure):
         ("buffers", ctypes.c_void_p * KAT_MAX_PEERS),
     ]
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 
 class KatPlan(ctypes.Structure):
@@ -100,6 +100,8 @@ class KatPlan(ctypes.Structure):
         ("max_segments", ctypes.c_int32),
         ("max_local_groups", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_uint64),
+        ("col_block_blocks", ctypes.c_int64),
+        ("col_block_extra", ctypes.c_int64),
     ]
 
     def as_dict(self) -> dict:

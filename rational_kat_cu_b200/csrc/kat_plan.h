@@ -4,10 +4,22 @@
 // namespace of kat_rational.cu after kat_rational.h, <stdint.h> and <string.h>.
 #pragma once
 
+#ifdef __CUDACC__
+#define KAT_PLAN_HD __host__ __device__ __forceinline__
+#else
+#define KAT_PLAN_HD inline
+#endif
+
 constexpr int kPlanSums = 10;      // fp64 partial sums per (block, segment, group): 6 + 4 moments
 constexpr int kMaxThreads = 512;  // block size cap
 constexpr int64_t kMaxElements = int64_t(1) << 48;
 constexpr int64_t kMaxBlocks = int64_t(1) << 14;
+// A block whose item range crosses a column-block boundary refills its loads from empty and
+// reduces twice: measured on B200 (x[5461, 3072] and x[25216, 3072] bf16 backward, 148 blocks)
+// such a block finishes 4.5-5 us after the others, about the time of 6 rows per thread of work
+// (the cp.async backward keeps 6 rows per thread in flight).  The planner gives each column
+// block whole blocks when that costs less than this many rows per thread.
+constexpr int kStraddleRows = 6;
 
 // Launch geometry shared by host and device (a POD copy of kat_rational_plan).
 struct Plan {
@@ -29,6 +41,11 @@ struct Plan {
   uint64_t workspace_bytes;
   int64_t items_q;     // items per block, floor(items / blocks)
   int64_t items_r;     // the first items_r blocks take one more item
+  // Split aligned to column blocks (cb_q > 0): the first cb_r column blocks get cb_q + 1
+  // blocks and the others cb_q; a column block's rows are split evenly over its blocks
+  // (rq_hi / rr_hi: quotient and remainder of rows by cb_q + 1, rq_lo / rr_lo: by cb_q).
+  // cb_q == 0: the items are split evenly over all blocks (items_q / items_r).
+  int64_t cb_q, cb_r, rq_hi, rr_hi, rq_lo, rr_lo;
   uint64_t rows_m;     // multiply-shift constants for dividing by rows ...
   uint64_t vg_m;       // ... and by vec_group
   int32_t rows_s1, rows_s2, vg_s1, vg_s2;
@@ -122,6 +139,19 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   const int64_t per_block = (p->items + blocks - 1) / blocks;
   int64_t segs = (per_block - 1) / batch + 2;
   if (segs > p->col_blocks) segs = p->col_blocks;
+  if (p->col_blocks > 1 && blocks >= p->col_blocks) {
+    const int64_t q = blocks / p->col_blocks;
+    const int64_t aligned = (batch + q - 1) / q;   // largest block of a column block with q
+    if (batch > q && aligned - per_block < int64_t(kStraddleRows) * p->tile_rows) {
+      p->cb_q = q;
+      p->cb_r = blocks % p->col_blocks;
+      p->rq_hi = batch / (q + 1);
+      p->rr_hi = batch % (q + 1);
+      p->rq_lo = batch / q;
+      p->rr_lo = batch % q;
+      segs = 1;
+    }
+  }
   p->max_segments = int32_t(segs);
   int64_t lg = (int64_t(p->tile_cols) - 1) / p->vec_group + 2;
   if (lg > num_groups) lg = num_groups;
@@ -134,3 +164,31 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   return KAT_OK;
 }
 
+
+// Item range [i0, i1) of block `blk`: an even split of all items (sizes differ by at most
+// one), or, when the plan aligns blocks to column blocks, an even split of one column block's
+// rows.  Every block gets at least one item.
+KAT_PLAN_HD void block_items(const Plan& p, int64_t blk, int64_t& i0, int64_t& i1) {
+  if (p.cb_q == 0) {
+    i0 = blk * p.items_q + (blk < p.items_r ? blk : p.items_r);
+    i1 = i0 + p.items_q + (blk < p.items_r ? 1 : 0);
+    return;
+  }
+  const int64_t hi = p.cb_q + 1;
+  const int64_t first_lo = p.cb_r * hi;   // first block of the column blocks with cb_q blocks
+  int64_t cb, k, rq, rr;
+  if (blk < first_lo) {
+    cb = blk / hi;
+    k = blk - cb * hi;
+    rq = p.rq_hi;
+    rr = p.rr_hi;
+  } else {
+    const int64_t j = (blk - first_lo) / p.cb_q;
+    cb = p.cb_r + j;
+    k = blk - first_lo - j * p.cb_q;
+    rq = p.rq_lo;
+    rr = p.rr_lo;
+  }
+  i0 = cb * p.rows + k * rq + (k < rr ? k : rr);
+  i1 = i0 + rq + (k < rr ? 1 : 0);
+}

@@ -100,12 +100,6 @@ __device__ __forceinline__ int64_t fast_div(int64_t n, uint64_t m, int32_t s1, i
 }
 
 
-// Item range [i0, i1) of block `blk` (even split, sizes differ by at most one).
-__device__ __forceinline__ void block_items(const Plan& p, int64_t blk, int64_t& i0, int64_t& i1) {
-  i0 = blk * p.items_q + min(blk, p.items_r);
-  i1 = i0 + p.items_q + (blk < p.items_r ? 1 : 0);
-}
-
 // Per-block, per-group reduction of one segment's per-thread sums (fixed order): thread t
 // of the `nthreads` participants stores its 10 sums (slot-major, rows padded by one float so
 // the slots fall in different banks), then each output (local group x slot) is added in
@@ -1234,6 +1228,8 @@ void to_public(const Plan& p, kat_rational_plan* out) {
   out->max_segments = p.max_segments;
   out->max_local_groups = p.max_local_groups;
   out->workspace_bytes = p.workspace_bytes;
+  out->col_block_blocks = p.cb_q;
+  out->col_block_extra = p.cb_r;
 }
 
 // Per-device SM count and per-(device, kernel, block size) occupancy caches.

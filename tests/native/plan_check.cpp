@@ -7,7 +7,8 @@
 //    here with a 128-bit product) for divisors 1 .. 2^62 and dividends up to 2^63 - 1;
 //  * make_plan_impl: every accepted plan covers each row and vector column exactly once, its
 //    blocks' item ranges tile [0, items), each block touches at most max_segments column
-//    blocks, each column block holds at most max_local_groups groups, the partial-sum
+//    blocks (one when the split is aligned to column blocks, whose blocks then differ by at
+//    most one item within a column block), each column block holds at most max_local_groups groups, the partial-sum
 //    workspace is exactly blocks x segments x local groups x 10 doubles, and the block size is
 //    a multiple of 32 within the cap.
 #include <stdint.h>
@@ -71,11 +72,11 @@ void check_divider(std::mt19937_64& rng) {
 }
 
 void block_range(const Plan& p, int64_t blk, int64_t* i0, int64_t* i1) {
-  *i0 = blk * p.items_q + (blk < p.items_r ? blk : p.items_r);
-  *i1 = *i0 + p.items_q + (blk < p.items_r ? 1 : 0);
+  block_items(p, blk, *i0, *i1);
 }
 
 int64_t plans_checked = 0;
+int64_t aligned_plans = 0;
 
 void check_plan(int64_t batch, int64_t channels, int64_t inner, int64_t groups, int dtype, int vec,
                 int sms, int ctas, int max_cols, int max_threads) {
@@ -111,6 +112,33 @@ void check_plan(int64_t batch, int64_t channels, int64_t inner, int64_t groups, 
     EXPECT(int64_t(host_fast_div(uint64_t(i0), p.rows_m, p.rows_s1, p.rows_s2)) == cb0, "cb0");
   }
   EXPECT(expect_i0 == p.items, "ranges tile the items");
+  if (p.cb_q > 0) {
+    // Aligned split: every block inside one column block, sizes within a column block differ
+    // by at most one, and the largest block is at most kStraddleRows tile rows above the even
+    // split's largest.
+    ++aligned_plans;
+    EXPECT(p.max_segments == 1, "aligned plan with %d segments", p.max_segments);
+    EXPECT(p.cb_q * p.col_blocks + p.cb_r == p.blocks && p.cb_r < p.col_blocks, "aligned counts");
+    const int64_t even_max = (p.items + p.blocks - 1) / p.blocks;
+    int64_t prev_cb = -1, lo = 0, hi = 0;
+    for (int64_t b = 0; b <= p.blocks; ++b) {
+      int64_t i0 = 0, i1 = 0, cb = -2;
+      if (b < p.blocks) {
+        block_range(p, b, &i0, &i1);
+        cb = i0 / p.rows;
+        EXPECT((i1 - 1) / p.rows == cb, "aligned block %lld crosses a column block", (long long)b);
+        EXPECT(i1 - i0 < even_max + int64_t(kStraddleRows) * p.tile_rows, "aligned block size");
+      }
+      if (cb != prev_cb) {
+        if (prev_cb >= 0) EXPECT(hi - lo <= 1, "column block %lld sizes %lld..%lld", (long long)prev_cb, (long long)lo, (long long)hi);
+        lo = hi = i1 - i0;
+        prev_cb = cb;
+      } else {
+        lo = i1 - i0 < lo ? i1 - i0 : lo;
+        hi = i1 - i0 > hi ? i1 - i0 : hi;
+      }
+    }
+  }
   for (int64_t cb = 0; cb < p.col_blocks; ++cb) {
     const int64_t col0 = cb * p.tile_cols;
     int64_t col_end = col0 + p.tile_cols;
@@ -168,6 +196,9 @@ int main() {
     fprintf(stderr, "%d failures\n", failures);
     return 1;
   }
-  printf("ok %lld plans\n", (long long)plans_checked);
+  EXPECT(aligned_plans > 0 && aligned_plans < plans_checked, "aligned plans %lld of %lld",
+         (long long)aligned_plans, (long long)plans_checked);
+  printf("ok %lld plans (%lld aligned to column blocks)\n", (long long)plans_checked,
+         (long long)aligned_plans);
   return 0;
 }

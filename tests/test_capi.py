@@ -146,9 +146,24 @@ def test_argument_errors_return_before_any_launch():
 # ---------------------------------------------------------------------------
 
 def block_items(p, blk):
-    q, r = divmod(p["items"], p["blocks"])
-    i0 = blk * q + min(blk, r)
-    return i0, i0 + q + (1 if blk < r else 0)
+    """Item range of block `blk`: an even split of all items, or (col_block_blocks > 0) an
+    even split of one column block's rows over that column block's blocks."""
+    cq = p["col_block_blocks"]
+    if cq == 0:
+        q, r = divmod(p["items"], p["blocks"])
+        i0 = blk * q + min(blk, r)
+        return i0, i0 + q + (1 if blk < r else 0)
+    cr = p["col_block_extra"]
+    counts = [cq + 1] * cr + [cq] * (p["col_blocks"] - cr)
+    first = 0
+    for cb, n in enumerate(counts):
+        if blk < first + n:
+            k = blk - first
+            q, r = divmod(p["rows"], n)
+            i0 = cb * p["rows"] + k * q + min(k, r)
+            return i0, i0 + q + (1 if k < r else 0)
+        first += n
+    raise AssertionError(f"block {blk} beyond the split")
 
 
 def simulate(p):
@@ -218,6 +233,9 @@ SHAPES = [
     (11, 36, 1, 12, 0, 2, 2),        # odd group width: scalar path
     (1, 4, 1, 2, 2, 2, 4),
     (64, 24, 5, 3, 0, 4, 4),
+    (50, 8192, 1, 8, 2, 7, 1),       # two column blocks, blocks aligned to them
+    (97, 16384, 1, 16, 0, 5, 2),     # eight column blocks, 10 blocks: an even split
+    (13, 8192, 1, 64, 0, 5, 1),      # four column blocks, 5 blocks: aligned, one extra
 ]
 
 
@@ -236,6 +254,24 @@ def test_plan_covers_every_element_once(shape):
     assert len(covered) == batch * vec_cols
     assert set(covered.values()) == {1}
     assert set(read) == set(written) and set(read.values()) == {1}
+
+
+def test_plan_aligns_blocks_to_column_blocks():
+    """A block that crosses a column-block boundary refills its loads and reduces twice; when
+    whole blocks per column block cost fewer than a few rows per thread, no block crosses."""
+    # x[5461, 8192] bf16 on 148 SMs: two column blocks of 512 vectors, 74 blocks each
+    p = _native.make_plan(5461, 8192, 1, 8, 2, sm_count=148, ctas_per_sm=1)
+    assert p["col_blocks"] == 2 and p["col_block_blocks"] == 74 and p["col_block_extra"] == 0
+    assert p["max_segments"] == 1
+    for b in range(p["blocks"]):
+        i0, i1 = block_items(p, b)
+        assert i0 // p["rows"] == (i1 - 1) // p["rows"]
+    sizes = [block_items(p, b)[1] - block_items(p, b)[0] for b in range(p["blocks"])]
+    assert max(sizes) - min(sizes) <= 1
+    # 64 column blocks of 640 rows on 148 blocks: two or three blocks per column block would
+    # give the largest block 320 rows against 277 evenly, more than a refill costs
+    p = _native.make_plan(640, 262144, 1, 8, 2, sm_count=148, ctas_per_sm=1)
+    assert p["col_blocks"] == 64 and p["col_block_blocks"] == 0
 
 
 def test_plan_vector_width_follows_group_width():
