@@ -487,8 +487,10 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
 // lane totals are added with a fixed xor tree, leaving the result in every lane.  The segments
 // of a block that hold group g are the column blocks cb0 .. cb1 of the block's item range that
 // meet the group's vector columns; the loads of four consecutive blocks of a lane are issued
-// before any of them is added, so a lane waits for memory once per four blocks (the order of
-// the additions is the block order all the same).
+// before any of them is added, so a lane waits for memory once per four blocks, and a block's
+// further segments of the group are loaded kSegAhead at a time (the order of the additions is
+// the block order, then the segment order, all the same: kSegAhead only sets how many loads
+// are in flight; 1 in the exchange kernel, whose block size leaves fewer registers).
 __device__ __forceinline__ const double* group_slot(const double* __restrict__ partial,
                                                     const Plan& p, int64_t blk, int64_t seg,
                                                     int64_t lg) {
@@ -499,6 +501,7 @@ __device__ __forceinline__ const double* group_slot(const double* __restrict__ p
   return src;
 }
 
+template <int kSegAhead = 4>
 __device__ __forceinline__ void group_totals(const double* __restrict__ partial, const Plan& p,
                                              int64_t g, int lane, double (&tot)[kAcc]) {
 #pragma unroll
@@ -538,13 +541,29 @@ __device__ __forceinline__ void group_totals(const double* __restrict__ partial,
       if (first[a] == nullptr) continue;
 #pragma unroll
       for (int k = 0; k < kAcc; ++k) tot[k] += v[a][k];
-      // further column blocks of this block that hold part of the group (wide groups)
-      for (int64_t cb = lo[a] + 1; cb <= hi[a]; ++cb) {
-        const int64_t gf = fast_div(cb * p.tile_cols, p.vg_m, p.vg_s1, p.vg_s2);
-        const double* src = group_slot(partial, p, b0 + 32 * a, cb - c0[a], g - gf);
-        if (src == nullptr) continue;
+      // further column blocks of this block that hold part of the group (wide groups): their
+      // loads are issued kSegAhead at a time before any of them is added, still added in
+      // column-block order
+      for (int64_t cb = lo[a] + 1; cb <= hi[a]; cb += kSegAhead) {
+        double w[kSegAhead][kAcc];
+        bool have[kSegAhead];
 #pragma unroll
-        for (int k = 0; k < kAcc; ++k) tot[k] += src[k];
+        for (int s = 0; s < kSegAhead; ++s) {
+          const double* src = nullptr;
+          if (cb + s <= hi[a]) {
+            const int64_t gf = fast_div((cb + s) * p.tile_cols, p.vg_m, p.vg_s1, p.vg_s2);
+            src = group_slot(partial, p, b0 + 32 * a, cb + s - c0[a], g - gf);
+          }
+          have[s] = src != nullptr;
+#pragma unroll
+          for (int k = 0; k < kAcc; ++k) w[s][k] = have[s] ? src[k] : 0.0;
+        }
+#pragma unroll
+        for (int s = 0; s < kSegAhead; ++s) {
+          if (!have[s]) continue;
+#pragma unroll
+          for (int k = 0; k < kAcc; ++k) tot[k] += w[s][k];
+        }
       }
     }
   }
@@ -1122,7 +1141,7 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
-    group_totals(partial, p, g, lane, tot);
+    group_totals<1>(partial, p, g, lane, tot);
 #pragma unroll
     for (int k = 0; k < kAcc; ++k)
       if (lane == k) s_sum[g * kAcc + k] = tot[k];
