@@ -486,11 +486,11 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
 // lane j takes blocks j, j+32, ... in order (each block's segments in order), then the 10
 // lane totals are added with a fixed xor tree, leaving the result in every lane.  The segments
 // of a block that hold group g are the column blocks cb0 .. cb1 of the block's item range that
-// meet the group's vector columns; the loads of four consecutive blocks of a lane are issued
-// before any of them is added, so a lane waits for memory once per four blocks, and a block's
-// further segments of the group are loaded kSegAhead at a time (the order of the additions is
-// the block order, then the segment order, all the same: kSegAhead only sets how many loads
-// are in flight; 1 in the exchange kernel, whose block size leaves fewer registers).
+// meet the group's vector columns; the loads of kAhead consecutive blocks of a lane are issued
+// before any of them is added, so a lane waits for memory once per kAhead blocks, and a
+// block's further segments of the group are loaded kSegAhead at a time.  The order of the
+// additions is the block order, then the segment order, whatever the two depths: they only set
+// how many loads are in flight (ReduceDepth below picks them per plan).
 __device__ __forceinline__ const double* group_slot(const double* __restrict__ partial,
                                                     const Plan& p, int64_t blk, int64_t seg,
                                                     int64_t lg) {
@@ -501,7 +501,7 @@ __device__ __forceinline__ const double* group_slot(const double* __restrict__ p
   return src;
 }
 
-template <int kSegAhead = 4>
+template <int kAhead, int kSegAhead>
 __device__ __forceinline__ void group_totals(const double* __restrict__ partial, const Plan& p,
                                              int64_t g, int lane, double (&tot)[kAcc]) {
 #pragma unroll
@@ -509,7 +509,6 @@ __device__ __forceinline__ void group_totals(const double* __restrict__ partial,
   // column blocks that meet group g's vector columns [g vg, (g + 1) vg)
   const int64_t cb_lo = (g * p.vec_group) / p.tile_cols;
   const int64_t cb_hi = ((g + 1) * p.vec_group - 1) / p.tile_cols;
-  constexpr int kAhead = 4;
   for (int64_t b0 = lane; b0 < p.blocks; b0 += 32 * kAhead) {
     int64_t lo[kAhead], hi[kAhead], c0[kAhead];
     const double* first[kAhead];
@@ -599,8 +598,16 @@ __device__ __forceinline__ void write_group(const double (&tot)[kAcc], double sc
   }
 }
 
+// Load depths of the grid reductions: with one segment per block (every block inside one
+// column block, the usual case) five blocks per lane cover a 148-block grid in one round of
+// loads; with several segments per block, four blocks and four further segments per round
+// (x[64,256,56,56] NCHW: ~11 segments of a group per block).  Same additions, same bits.
+struct DepthOneSegment { static constexpr int kAhead = 5, kSeg = 1; };
+struct DepthSegments { static constexpr int kAhead = 4, kSeg = 4; };
+
 // Grid reduction: one warp per group.
 constexpr int kReduceWarps = 8;
+template <typename Depth>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restrict__ den,
                       float* __restrict__ dnum, float* __restrict__ dden, const Plan p) {
@@ -611,13 +618,14 @@ kat_bwd_reduce_kernel(const double* __restrict__ partial, const float* __restric
   // has completed and its stores are visible (returns at once for an ordinary launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   double tot[kAcc];
-  group_totals(partial, p, g, lane, tot);
+  group_totals<Depth::kAhead, Depth::kSeg>(partial, p, g, lane, tot);
   write_group(tot, 1.0, true, g, lane, den, dnum, dden, p.formula);
 }
 
 // The same with one numerator row shared by every group: one block; warp w takes groups
 // w, w + 8, ... in order, writes their denominator gradients and adds their numerator totals;
 // the 8 warp sums are then added in warp order (fp64) and rounded once into dnum[0..5].
+template <typename Depth>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 kat_bwd_reduce_shared_kernel(const double* __restrict__ partial, const float* __restrict__ den,
                              float* __restrict__ dnum, float* __restrict__ dden, const Plan p) {
@@ -628,7 +636,7 @@ kat_bwd_reduce_shared_kernel(const double* __restrict__ partial, const float* __
   double num_sum = 0.0;   // lane k < 6: numerator moment k over this warp's groups
   for (int64_t g = warp; g < p.num_groups; g += kReduceWarps) {
     double tot[kAcc];
-    group_totals(partial, p, g, lane, tot);
+    group_totals<Depth::kAhead, Depth::kSeg>(partial, p, g, lane, tot);
 #pragma unroll
     for (int k = 0; k < 6; ++k)
       if (lane == k) num_sum += tot[k];
@@ -1141,7 +1149,7 @@ kat_bwd_reduce_exchange_kernel(const double* __restrict__ partial, const float* 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int g = warp; g < G; g += nwarps) {
     double tot[kAcc];
-    group_totals<1>(partial, p, g, lane, tot);
+    group_totals<4, 1>(partial, p, g, lane, tot);
 #pragma unroll
     for (int k = 0; k < kAcc; ++k)
       if (lane == k) s_sum[g * kAcc + k] = tot[k];
@@ -1845,17 +1853,26 @@ cudaError_t launch_bwd_tma(int dtype, const void* x, const void* gy, void* dx, c
 
 int launch_reduce(const void* workspace, const float* den, float* dnum, float* dden,
                   const Plan& p, const Peers* peers, cudaStream_t s) {
+  const bool one_segment = p.max_segments == 1;
+  const double* partial = static_cast<const double*>(workspace);
   if (peers == nullptr && p.num_stride == 0) {
-    if (launch_pdl(kat_bwd_reduce_shared_kernel, dim3(1), dim3(kReduceWarps * 32), 0, s,
-                   static_cast<const double*>(workspace), den, dnum, dden, p) != cudaSuccess)
-      return KAT_ERR_CUDA;
+    const cudaError_t e =
+        one_segment
+            ? launch_pdl(kat_bwd_reduce_shared_kernel<DepthOneSegment>, dim3(1),
+                         dim3(kReduceWarps * 32), 0, s, partial, den, dnum, dden, p)
+            : launch_pdl(kat_bwd_reduce_shared_kernel<DepthSegments>, dim3(1),
+                         dim3(kReduceWarps * 32), 0, s, partial, den, dnum, dden, p);
+    if (e != cudaSuccess) return KAT_ERR_CUDA;
   } else if (peers == nullptr) {
     // Programmatic dependent launch: the reduction's launch overlaps the tail of the
     // partial-sum kernel, and griddepcontrol.wait inside it orders the reads.
     const unsigned grid = unsigned((p.num_groups + kReduceWarps - 1) / kReduceWarps);
-    if (launch_pdl(kat_bwd_reduce_kernel, dim3(grid), dim3(kReduceWarps * 32), 0, s,
-                   static_cast<const double*>(workspace), den, dnum, dden, p) != cudaSuccess)
-      return KAT_ERR_CUDA;
+    const cudaError_t e =
+        one_segment ? launch_pdl(kat_bwd_reduce_kernel<DepthOneSegment>, dim3(grid),
+                                 dim3(kReduceWarps * 32), 0, s, partial, den, dnum, dden, p)
+                    : launch_pdl(kat_bwd_reduce_kernel<DepthSegments>, dim3(grid),
+                                 dim3(kReduceWarps * 32), 0, s, partial, den, dnum, dden, p);
+    if (e != cudaSuccess) return KAT_ERR_CUDA;
   } else {
     const size_t smem = size_t(p.num_groups) * kAcc * sizeof(double);
     if (smem > 48 * 1024) {
