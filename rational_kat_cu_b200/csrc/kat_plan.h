@@ -164,7 +164,6 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   return KAT_OK;
 }
 
-
 // Item range [i0, i1) of block `blk`: an even split of all items (sizes differ by at most
 // one), or, when the plan aligns blocks to column blocks, an even split of one column block's
 // rows.  Every block gets at least one item.
