@@ -41,8 +41,17 @@
 namespace {
 
 constexpr int kTileCols = 32;   // features per tile (one warp)
-constexpr int kTileRows = 8;    // batch rows per tile (one per warp)
-constexpr int kBsThreads = kTileCols * kTileRows;
+constexpr int kWarps = 8;       // warps per block; warp w takes rows w R .. w R + R - 1 of a tile
+constexpr int kBsThreads = kTileCols * kWarps;
+// Rows per warp and tile (R): the knot counts of the default cubic layers (grid 5 and 8: 12 and
+// 15 knots) are compiled in and take R = 4 or 2 rows per warp, so a warp's loop, column and
+// copy bookkeeping is paid once per R elements per lane and its R x loads are in flight
+// together; any other order or knot count runs with the knot count at run time and 1 row per
+// warp.  R = 4 where four blocks still fit in an SM's shared memory, else 2 (x[16384,1024]
+// fp32 on one B200, forward / backward: grid 5 at R = 4 154 / 138 us, at R = 2 160 / 147;
+// grid 8, 61.5 KB per block at R = 4, 197 / 158 us there and 177 / 161 at R = 2; R = 8 slower
+// for both; 226 / 212 and 223 / 203 us with one row per warp and the knot count at run time).
+constexpr size_t kFourBlocksSmem = 56 * 1024;
 constexpr int kMaxOrder = 5;
 constexpr int kMaxKnots = 64;
 constexpr float kEps = 1e-8f;
@@ -66,14 +75,14 @@ struct Smem {
   float* knots;
   float* recip;
   float* diff;
-  float* slab;    // [8][32 * n_basis]
+  float* slab;    // [8 warps][R rows][32 * n_basis]
 };
 
-size_t smem_bytes(int n_knots, int order) {
+size_t smem_bytes(int n_knots, int order, int rows_per_warp) {
   const int nb = n_knots - 1 - order;
   return sizeof(float) * kTileCols *
          (size_t(n_knots + 2 * order) + 2 * size_t(order) * (n_knots + order) +
-          size_t(kTileRows) * nb);
+          size_t(kWarps) * rows_per_warp * nb);
 }
 
 template <int kOrder>
@@ -123,9 +132,16 @@ __device__ __forceinline__ void load_column(const Smem& sm, const float* __restr
 // Largest i in [0, n - 2] with t_i <= x, for t_0 <= x < t_{n-1} (non-decreasing t), by binary
 // search over the bits of i (a fixed number of steps, no data-dependent branches); knot t_j of
 // this lane's feature is t[j * 32].
+__host__ __device__ constexpr int pow2_floor(int v) {
+  int p = 1;
+  while (p * 2 <= v) p *= 2;
+  return p;
+}
+template <int kKnots>   // the knot count when compiled in (> 0), else n at run time
 __device__ __forceinline__ int find_span(const float* t, int n, float x) {
   int i = 0;
-  for (int step = 1 << (31 - __clz(n - 2)); step > 0; step >>= 1) {
+  const int top = kKnots > 0 ? pow2_floor(kKnots - 2) : 1 << (31 - __clz(n - 2));
+  for (int step = top; step > 0; step >>= 1) {
     const int c = i + step;
     if (c <= n - 2 && t[c * kTileCols] <= x) i = c;
   }
@@ -196,8 +212,44 @@ __device__ __forceinline__ void span_basis(const float (&xl)[kOrder], const floa
   if constexpr (kLevels == 0) b[0] = 1.0f;
 }
 
+// One forward element: the basis values of x = v of this lane's feature scattered into its
+// zeroed slab row r (n_basis floats): NaN in every value for a non-finite x, the k + 1 values of
+// its span inside [t_0, t_{n-1}), nothing (zeros) outside.
+template <int kOrder, int kKnots>
+__device__ __forceinline__ void fwd_element(const Smem& sm, int lane, int n_knots, int nb, float v,
+                                            float* r) {
+  const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
+  if (!isfinite(v)) {
+    for (int j = 0; j < nb; ++j) r[j] = __int_as_float(0x7fc00000);
+  } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
+    const int i = find_span<kKnots>(t, n_knots, v);
+    float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
+    load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl, xr,
+                      rw, dw);
+    float b[kMaxOrder + 1];
+    span_basis<kOrder, kOrder>(xl, xr, rw, dw, n_knots, i, b);
+#pragma unroll
+    for (int m = 0; m <= kOrder; ++m) {
+      const int j = i - kOrder + m;
+      if (j >= 0 && j < nb) r[j] = b[m];
+    }
+  }
+}
+
+// 16-byte global -> shared copy that bypasses the registers (completed by cp_async_wait_all).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Warp-wide copy of `count` floats between a tile row's slab (16-byte aligned) and global
-// memory: 16-byte accesses when the global side is 16-byte aligned, else 4-byte ones.
+// memory: 16-byte accesses when the global side is 16-byte aligned (towards shared memory as
+// cp.async copies, all in flight until the caller's cp_async_wait_all), else 4-byte ones.
 template <bool kToGlobal>
 __device__ __forceinline__ void warp_copy(float* __restrict__ slab, float* __restrict__ g,
                                           int count, int lane) {
@@ -206,7 +258,7 @@ __device__ __forceinline__ void warp_copy(float* __restrict__ slab, float* __res
     float4* s4 = reinterpret_cast<float4*>(slab);
     float4* g4 = reinterpret_cast<float4*>(g);
     for (int q = lane; q < c4; q += 32) {
-      if constexpr (kToGlobal) g4[q] = s4[q]; else s4[q] = __ldg(g4 + q);
+      if constexpr (kToGlobal) g4[q] = s4[q]; else cp_async16(s4 + q, g4 + q);
     }
     for (int q = (c4 << 2) + lane; q < count; q += 32) {
       if constexpr (kToGlobal) g[q] = slab[q]; else slab[q] = __ldg(g + q);
@@ -231,121 +283,149 @@ __device__ __forceinline__ void block_tiles(int64_t n_tiles, int64_t& t0, int64_
   t1 = t0 + q + (b < r ? 1 : 0);
 }
 
-template <int kOrder>
+// Tiles of kWarps R rows x 32 features; warp w owns rows w R .. w R + R - 1 of a tile.
+template <int kOrder, int kKnots, int kR>
 __global__ void __launch_bounds__(kBsThreads)
 kat_bspline_fwd_kernel(const float* __restrict__ x, const float* __restrict__ grid,
-                       float* __restrict__ out, int64_t batch, int64_t features, int n_knots) {
+                       float* __restrict__ out, int64_t batch, int64_t features, int knots_arg) {
   extern __shared__ __align__(16) float smem[];
+  constexpr int kTR = kWarps * kR;
+  const int n_knots = kKnots > 0 ? kKnots : knots_arg;
   const int nb = n_knots - 1 - kOrder;
+  const int row_floats = kTileCols * nb;   // one slab row: 32 features x n_basis
   const Smem sm = carve<kOrder>(smem, n_knots);
-  const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
+  const int64_t row_tiles = (batch + kTR - 1) / kTR;
   const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
   int64_t t0, t1;
   block_tiles(row_tiles * col_tiles, t0, t1);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float* const swarp = sm.slab + w * (kR * row_floats);
   int64_t loaded = -1;
   // (column tile, row tile) of tile t0, then advanced one tile at a time (no division per tile)
   int64_t ct = t0 / row_tiles, rt = t0 - (t0 / row_tiles) * row_tiles;
   for (int64_t tile = t0; tile < t1; ++tile) {
-    const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
+    const int64_t c0 = ct * kTileCols, row0 = rt * kTR + w * kR;
     const int ncols = int(min(int64_t(kTileCols), features - c0));
     if (ct != loaded) {
       __syncthreads();   // the previous column's tables are no longer read
       load_column<kOrder>(sm, grid, features, n_knots, c0);
       loaded = ct;
     }
-    float* srow = sm.slab + w * (kTileCols * nb);
-    {
-      float4* s4 = reinterpret_cast<float4*>(srow);   // 32 * nb floats: a multiple of 4
-      for (int q = lane; q < (kTileCols * nb) >> 2; q += 32) s4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    __syncwarp();
-    if (row < batch && lane < ncols) {
-      const float v = x[row * features + c0 + lane];
-      const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
-      float* r = srow + lane * nb;
-      if (!isfinite(v)) {
-        for (int j = 0; j < nb; ++j) r[j] = __int_as_float(0x7fc00000);
-      } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
-        const int i = find_span(t, n_knots, v);
-        float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
-        load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
-                          xr, rw, dw);
-        float b[kMaxOrder + 1];
-        span_basis<kOrder, kOrder>(xl, xr, rw, dw, n_knots, i, b);
+    // the warp's R x values, loaded before any is used
+    float v[kR];
 #pragma unroll
-        for (int m = 0; m <= kOrder; ++m) {
-          const int j = i - kOrder + m;
-          if (j >= 0 && j < nb) r[j] = b[m];
-        }
-      }
+    for (int r = 0; r < kR; ++r)
+      v[r] = (row0 + r < batch && lane < ncols) ? x[(row0 + r) * features + c0 + lane] : 0.0f;
+    {
+      float4* s4 = reinterpret_cast<float4*>(swarp);   // R x 32 x nb floats: a multiple of 4
+      for (int q = lane; q < (kR * row_floats) >> 2; q += 32) s4[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncwarp();
-    if (row < batch) warp_copy<true>(srow, out + row_offset(row, features, c0, nb), ncols * nb, lane);
+#pragma unroll
+    for (int r = 0; r < kR; ++r)
+      if (row0 + r < batch && lane < ncols)
+        fwd_element<kOrder, kKnots>(sm, lane, n_knots, nb, v[r], swarp + r * row_floats + lane * nb);
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      if (row0 + r >= batch) continue;
+      float* g = out + row_offset(row0 + r, features, c0, nb);
+      if (kKnots > 0 && ncols == kTileCols)   // a full tile: a compile-time count
+        warp_copy<true>(swarp + r * row_floats, g, kTileCols * (kKnots - 1 - kOrder), lane);
+      else
+        warp_copy<true>(swarp + r * row_floats, g, ncols * nb, lane);
+    }
     __syncwarp();
     if (++rt == row_tiles) { rt = 0; ++ct; }
   }
 }
 
-template <int kOrder>
+// One backward element: dx for x = v of this lane's feature from its incoming-gradient row r
+// (n_basis floats): NaN for a non-finite x, 0 outside [t_0, t_{n-1}).
+template <int kOrder, int kKnots>
+__device__ __forceinline__ float bwd_element(const Smem& sm, int lane, int n_knots, int nb,
+                                             float v, const float* r) {
+  const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
+  float acc = 0.0f;
+  if (!isfinite(v)) {
+    acc = __int_as_float(0x7fc00000);
+  } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
+    const int i = find_span<kKnots>(t, n_knots, v);
+    float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
+    load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl, xr,
+                      rw, dw);
+    // dB^K_j / dx = K (B^{K-1}_j / d_j - B^{K-1}_{j+1} / d_{j+1}), d_j = max(t_{j+K} - t_j,
+    // eps): the derivative autograd takes through the recursion, from the order K - 1 values
+    // (b[m'] = B^{K-1}_{i-K+1+m'}) and the level-K reciprocals.
+    float b[kMaxOrder + 1];
+    span_basis<kOrder, kOrder - 1>(xl, xr, rw, dw, n_knots, i, b);
+#pragma unroll
+    for (int m = 0; m <= kOrder; ++m) {
+      const int j = i - kOrder + m;
+      if (j >= 0 && j < nb) {
+        const float left = m >= 1 ? __fmul_rn(b[m - 1], rw[kOrder - 1][m - 1]) : 0.0f;
+        const float right = m <= kOrder - 1 ? __fmul_rn(b[m], rw[kOrder - 1][m]) : 0.0f;
+        const float d = __fmul_rn(float(kOrder), __fsub_rn(left, right));
+        acc = __fadd_rn(acc, __fmul_rn(r[j], d));
+      }
+    }
+  }
+  return acc;
+}
+
+template <int kOrder, int kKnots, int kR>
 __global__ void __launch_bounds__(kBsThreads)
 kat_bspline_bwd_kernel(const float* __restrict__ x, const float* __restrict__ grid,
                        const float* __restrict__ gb, float* __restrict__ gx, int64_t batch,
-                       int64_t features, int n_knots) {
+                       int64_t features, int knots_arg) {
   extern __shared__ __align__(16) float smem[];
+  constexpr int kTR = kWarps * kR;
+  const int n_knots = kKnots > 0 ? kKnots : knots_arg;
   const int nb = n_knots - 1 - kOrder;
+  const int row_floats = kTileCols * nb;
   const Smem sm = carve<kOrder>(smem, n_knots);
-  const int64_t row_tiles = (batch + kTileRows - 1) / kTileRows;
+  const int64_t row_tiles = (batch + kTR - 1) / kTR;
   const int64_t col_tiles = (features + kTileCols - 1) / kTileCols;
   int64_t t0, t1;
   block_tiles(row_tiles * col_tiles, t0, t1);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float* const swarp = sm.slab + w * (kR * row_floats);
   int64_t loaded = -1;
   // (column tile, row tile) of tile t0, then advanced one tile at a time (no division per tile)
   int64_t ct = t0 / row_tiles, rt = t0 - (t0 / row_tiles) * row_tiles;
   for (int64_t tile = t0; tile < t1; ++tile) {
-    const int64_t c0 = ct * kTileCols, row = rt * kTileRows + w;
+    const int64_t c0 = ct * kTileCols, row0 = rt * kTR + w * kR;
     const int ncols = int(min(int64_t(kTileCols), features - c0));
     if (ct != loaded) {
       __syncthreads();
       load_column<kOrder>(sm, grid, features, n_knots, c0);
       loaded = ct;
     }
-    float* srow = sm.slab + w * (kTileCols * nb);
-    if (row < batch)
-      warp_copy<false>(srow, const_cast<float*>(gb) + row_offset(row, features, c0, nb), ncols * nb,
-                       lane);
-    __syncwarp();
-    if (row < batch && lane < ncols) {
-      const float v = x[row * features + c0 + lane];
-      const float* t = sm.knots + kOrder * kTileCols + lane;   // t_j at t[j * 32]
-      const float* r = srow + lane * nb;
-      float acc = 0.0f;
-      if (!isfinite(v)) {
-        acc = __int_as_float(0x7fc00000);
-      } else if (v >= t[0] && v < t[(n_knots - 1) * kTileCols]) {
-        const int i = find_span(t, n_knots, v);
-        float xl[kOrder], xr[kOrder], rw[kOrder][kOrder], dw[kOrder][kOrder];
-        load_span<kOrder>(sm.knots + lane, sm.recip + lane, sm.diff + lane, n_knots, i, v, xl,
-                          xr, rw, dw);
-        // dB^K_j / dx = K (B^{K-1}_j / d_j - B^{K-1}_{j+1} / d_{j+1}), d_j = max(t_{j+K} - t_j,
-        // eps): the derivative autograd takes through the recursion, from the order K - 1 values
-        // (b[m'] = B^{K-1}_{i-K+1+m'}) and the level-K reciprocals.
-        float b[kMaxOrder + 1];
-        span_basis<kOrder, kOrder - 1>(xl, xr, rw, dw, n_knots, i, b);
+    // with several rows, the warp's x loads are issued before the incoming-gradient copies
+    float v[kR];
+    auto load_x = [&]() {
 #pragma unroll
-        for (int m = 0; m <= kOrder; ++m) {
-          const int j = i - kOrder + m;
-          if (j >= 0 && j < nb) {
-            const float left = m >= 1 ? __fmul_rn(b[m - 1], rw[kOrder - 1][m - 1]) : 0.0f;
-            const float right = m <= kOrder - 1 ? __fmul_rn(b[m], rw[kOrder - 1][m]) : 0.0f;
-            const float d = __fmul_rn(float(kOrder), __fsub_rn(left, right));
-            acc = __fadd_rn(acc, __fmul_rn(r[j], d));
-          }
-        }
-      }
-      gx[row * features + c0 + lane] = acc;
+      for (int r = 0; r < kR; ++r)
+        v[r] = (row0 + r < batch && lane < ncols) ? x[(row0 + r) * features + c0 + lane] : 0.0f;
+    };
+    if constexpr (kR > 1) load_x();
+#pragma unroll
+    for (int r = 0; r < kR; ++r) {
+      if (row0 + r >= batch) continue;
+      float* g = const_cast<float*>(gb) + row_offset(row0 + r, features, c0, nb);
+      if (kKnots > 0 && ncols == kTileCols)   // a full tile: a compile-time count
+        warp_copy<false>(swarp + r * row_floats, g, kTileCols * (kKnots - 1 - kOrder), lane);
+      else
+        warp_copy<false>(swarp + r * row_floats, g, ncols * nb, lane);
     }
+    cp_async_wait_all();
+    __syncwarp();
+    if constexpr (kR == 1) load_x();
+#pragma unroll
+    for (int r = 0; r < kR; ++r)
+      if (row0 + r < batch && lane < ncols)
+        gx[(row0 + r) * features + c0 + lane] =
+            bwd_element<kOrder, kKnots>(sm, lane, n_knots, nb, v[r], swarp + r * row_floats + lane * nb);
     __syncwarp();
     if (++rt == row_tiles) { rt = 0; ++ct; }
   }
@@ -361,7 +441,7 @@ int validate(int64_t batch, int64_t features, int32_t n_knots, int32_t order, in
 }
 
 // Grid: as many blocks as fit on the GPU at once, never more than there are tiles.
-cudaError_t grid_size(int64_t batch, int64_t features, const void* fn, size_t smem,
+cudaError_t grid_size(int64_t batch, int64_t features, int tile_rows, const void* fn, size_t smem,
                       unsigned* blocks) {
   int dev = 0, sms = 0, occ = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -370,35 +450,67 @@ cudaError_t grid_size(int64_t batch, int64_t features, const void* fn, size_t sm
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kBsThreads, smem);
   if (e != cudaSuccess) return e;
-  const int64_t tiles = ((batch + kTileRows - 1) / kTileRows) *
+  const int64_t tiles = ((batch + tile_rows - 1) / tile_rows) *
                         ((features + kTileCols - 1) / kTileCols);
   *blocks = unsigned(std::max<int64_t>(1, std::min<int64_t>(tiles, int64_t(sms) * std::max(occ, 1))));
   return cudaSuccess;
 }
 
+template <int kOrder, int kKnots, int kR>
+cudaError_t launch_fwd_k(const float* x, const float* grid, float* out, int64_t batch, int64_t f,
+                         int nk, cudaStream_t s) {
+  const size_t smem = smem_bytes(nk, kOrder, kR);
+  auto kernel = kat_bspline_fwd_kernel<kOrder, kKnots, kR>;
+  unsigned blocks = 0;
+  const cudaError_t e = grid_size(batch, f, kWarps * kR, (const void*)kernel, smem, &blocks);
+  if (e != cudaSuccess) return e;
+  kernel<<<blocks, kBsThreads, smem, s>>>(x, grid, out, batch, f, nk);
+  return cudaGetLastError();
+}
+
+template <int kOrder, int kKnots, int kR>
+cudaError_t launch_bwd_k(const float* x, const float* grid, const float* gb, float* gx,
+                         int64_t batch, int64_t f, int nk, cudaStream_t s) {
+  const size_t smem = smem_bytes(nk, kOrder, kR);
+  auto kernel = kat_bspline_bwd_kernel<kOrder, kKnots, kR>;
+  unsigned blocks = 0;
+  const cudaError_t e = grid_size(batch, f, kWarps * kR, (const void*)kernel, smem, &blocks);
+  if (e != cudaSuccess) return e;
+  kernel<<<blocks, kBsThreads, smem, s>>>(x, grid, gb, gx, batch, f, nk);
+  return cudaGetLastError();
+}
+
+// Rows per warp of the compiled-in cubic kernel for `knots` knots (see kFourBlocksSmem).
+constexpr int rows_for(int knots) {
+  return sizeof(float) * kTileCols *
+                     (size_t(knots + 6) + 6 * size_t(knots + 3) +
+                      size_t(kWarps) * 4 * (knots - 4)) <= kFourBlocksSmem
+             ? 4
+             : 2;
+}
+
+// Cubic layers with grid 5 or 8 (12 or 15 knots) take the compiled-in kernels; every other
+// order and knot count the general ones.
 template <int kOrder>
 cudaError_t launch_fwd(const float* x, const float* grid, float* out, int64_t batch, int64_t f,
                        int nk, cudaStream_t s) {
-  const size_t smem = smem_bytes(nk, kOrder);
-  unsigned blocks = 0;
-  const cudaError_t e = grid_size(batch, f, (const void*)kat_bspline_fwd_kernel<kOrder>, smem,
-                                  &blocks);
-  if (e != cudaSuccess) return e;
-  kat_bspline_fwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, out, batch, f, nk);
-  return cudaGetLastError();
+  if constexpr (kOrder == 3) {
+    if (nk == 12) return launch_fwd_k<3, 12, rows_for(12)>(x, grid, out, batch, f, nk, s);
+    if (nk == 15) return launch_fwd_k<3, 15, rows_for(15)>(x, grid, out, batch, f, nk, s);
+  }
+  return launch_fwd_k<kOrder, 0, 1>(x, grid, out, batch, f, nk, s);
 }
 
 template <int kOrder>
 cudaError_t launch_bwd(const float* x, const float* grid, const float* gb, float* gx,
                        int64_t batch, int64_t f, int nk, cudaStream_t s) {
-  const size_t smem = smem_bytes(nk, kOrder);
-  unsigned blocks = 0;
-  const cudaError_t e = grid_size(batch, f, (const void*)kat_bspline_bwd_kernel<kOrder>, smem,
-                                  &blocks);
-  if (e != cudaSuccess) return e;
-  kat_bspline_bwd_kernel<kOrder><<<blocks, kBsThreads, smem, s>>>(x, grid, gb, gx, batch, f, nk);
-  return cudaGetLastError();
+  if constexpr (kOrder == 3) {
+    if (nk == 12) return launch_bwd_k<3, 12, rows_for(12)>(x, grid, gb, gx, batch, f, nk, s);
+    if (nk == 15) return launch_bwd_k<3, 15, rows_for(15)>(x, grid, gb, gx, batch, f, nk, s);
+  }
+  return launch_bwd_k<kOrder, 0, 1>(x, grid, gb, gx, batch, f, nk, s);
 }
+static_assert(rows_for(12) == 4 && rows_for(15) == 2, "cubic grid 5 / grid 8 rows per warp");
 
 }  // namespace
 

@@ -68,6 +68,9 @@ def test_golden_cases(name, cuda_device):
 @pytest.mark.parametrize("B,D,grid_size,order", [
     (4, 32, 8, 3), (16, 128, 8, 3), (1, 64, 8, 3), (4, 32, 5, 3), (4, 64, 3, 2),
     (257, 33, 7, 1), (64, 100, 10, 4), (9, 17, 30, 5),
+    # cubic grid 8 / grid 5 (the kernels with the knot count compiled in, 32-row tiles):
+    # batches that end inside a warp's rows, ragged feature columns, several column tiles
+    (37, 45, 8, 3), (33, 70, 5, 3), (70, 64, 8, 3), (5, 96, 5, 3), (129, 31, 8, 3),
 ])
 def test_random_inputs(B, D, grid_size, order, cuda_device):
     g = torch.Generator().manual_seed(B * D + order)
