@@ -99,7 +99,6 @@ __device__ __forceinline__ int64_t fast_div(int64_t n, uint64_t m, int32_t s1, i
   return int64_t((t + ((un - t) >> s1)) >> s2);
 }
 
-
 // Per-block, per-group reduction of one segment's per-thread sums (fixed order): thread t
 // of the `nthreads` participants stores its 10 sums (slot-major, rows padded by one float so
 // the slots fall in different banks), then each output (local group x slot) is added in
@@ -490,7 +489,8 @@ kat_bwd_async_kernel(const Tio* __restrict__ x, const Tio* __restrict__ gy, Tio*
 // before any of them is added, so a lane waits for memory once per kAhead blocks, and a
 // block's further segments of the group are loaded kSegAhead at a time.  The order of the
 // additions is the block order, then the segment order, whatever the two depths: they only set
-// how many loads are in flight (ReduceDepth below picks them per plan).
+// how many loads are in flight (DepthOneSegment / DepthSegments below; launch_reduce picks one
+// per plan).
 __device__ __forceinline__ const double* group_slot(const double* __restrict__ partial,
                                                     const Plan& p, int64_t blk, int64_t seg,
                                                     int64_t lg) {
