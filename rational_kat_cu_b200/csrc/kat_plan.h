@@ -164,6 +164,19 @@ int make_plan_impl(int64_t batch, int64_t channels, int64_t inner, int64_t num_g
   return KAT_OK;
 }
 
+// Extra load-ring refills a plan costs, as a fraction of a thread's rows: a block refills its
+// ring at every column block it enters after the first (kStraddleRows rows of work each), and
+// works through per_block / tile_rows rows per thread.  Short, wide problems (few rows, many
+// column blocks: x[64,256,56,56] NCHW is 64 rows of 200,704 vectors) pay several refills per
+// block with narrow tiles; the cp.async backward's planner compares tile widths with it.
+inline double refill_overhead(const Plan& p) {
+  if (p.items == 0 || p.blocks == 0 || p.rows == 0) return 0.0;
+  const double per_block = double(p.items) / double(p.blocks);
+  const double segments = p.cb_q > 0 ? 1.0 : per_block / double(p.rows) + 1.0;
+  const double rows_per_thread = per_block / double(p.tile_rows);
+  return (segments - 1.0) * kStraddleRows / rows_per_thread;
+}
+
 // Item range [i0, i1) of block `blk`: an even split of all items (sizes differ by at most
 // one), or, when the plan aligns blocks to column blocks, an even split of one column block's
 // rows.  Every block gets at least one item.

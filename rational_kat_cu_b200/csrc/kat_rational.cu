@@ -1765,13 +1765,40 @@ int plan_async_uncached(int64_t batch, int64_t channels, int64_t inner, int64_t 
   if (cudaGetDevice(&dev) != cudaSuccess) return KAT_ERR_CUDA;
   int sms = 0;
   if (device_sm_count(dev, &sms) != cudaSuccess) return KAT_ERR_CUDA;
-  // Block shape of the cp.async backward: at most kAsyncCols vector columns, and as many
-  // rows as fill kMaxThreads threads (at 128 registers, one 512-thread block per SM).
-  static const int max_cols =
-      std::max(32, std::min(env_int("KAT_RATIONAL_ASYNC_COLS", kAsyncCols), kAsyncThreads) / 32 * 32);
+  // Block shape of the cp.async backward: at most max_cols vector columns, and as many rows as
+  // fill kAsyncThreads threads (at 128 registers, one 512-thread block per SM).  kAsyncCols
+  // (128 columns x 4 rows) unless a wider tile of full blocks needs fewer ring refills
+  // (refill_overhead, by more than 2% of a thread's rows): short, wide problems such as
+  // x[64,256,56,56] NCHW, whose blocks cross ~11 column blocks of 64 rows at 128 columns
+  // (backward 140 us there against 111 us at 512 columns on one B200).  KAT_RATIONAL_ASYNC_COLS
+  // pins the width.
+  static const int env_cols = env_int("KAT_RATIONAL_ASYNC_COLS", 0);
+  int max_cols = kAsyncCols;
   Plan probe;
-  int st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
-                          max_cols, kAsyncThreads);
+  int st = KAT_OK;
+  if (env_cols > 0) {
+    max_cols = std::max(32, std::min(env_cols, kAsyncThreads) / 32 * 32);
+    st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
+                        max_cols, kAsyncThreads);
+  } else {
+    st = make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &probe,
+                        max_cols, kAsyncThreads);
+    if (st != KAT_OK) return st;
+    double best = refill_overhead(probe);
+    for (int cols = 2 * kAsyncCols; cols <= kAsyncThreads; cols *= 2) {
+      Plan wide;
+      if (make_plan_impl(batch, channels, inner, num_groups, dtype, vmax, sms, 1, &wide, cols,
+                         kAsyncThreads) != KAT_OK ||
+          wide.threads != probe.threads)
+        continue;
+      const double ov = refill_overhead(wide);
+      if (ov < best - 0.02) {
+        best = ov;
+        max_cols = cols;
+        probe = wide;
+      }
+    }
+  }
   if (st != KAT_OK) return st;
   const void* fn = bwd_async_kernel_for(dtype, formula, vb);
   const size_t smem = async_smem_bytes(probe.threads, vb);

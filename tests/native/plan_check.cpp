@@ -184,6 +184,23 @@ int main() {
                int(rng() % 2 ? 0 : 1 << (rng() % 4)), int(1 + rng() % 200), int(1 + rng() % 4),
                int(32 * (1 + rng() % 16)), int(32 * (1 + rng() % 20)));
   }
+  // Refill estimate behind the cp.async backward's tile width: x[64,256,56,56] fp32 NCHW
+  // (64 rows of 200,704 vectors) crosses ~11 column blocks per block at 128 columns and ~3 at
+  // 512; x[25216, 3072] bf16 has one column block per block at 128 columns (aligned split).
+  {
+    Plan narrow, wide, headline;
+    EXPECT(make_plan_impl(64, 256, 3136, 8, KAT_DTYPE_F32, 4, 148, 1, &narrow, 128, 512) == KAT_OK &&
+               make_plan_impl(64, 256, 3136, 8, KAT_DTYPE_F32, 4, 148, 1, &wide, 512, 512) == KAT_OK,
+           "NCHW plans");
+    EXPECT(narrow.threads == 512 && wide.threads == 512, "full blocks");
+    EXPECT(refill_overhead(narrow) > 0.3 && refill_overhead(wide) < 0.12 &&
+               refill_overhead(wide) < refill_overhead(narrow) - 0.02,
+           "NCHW refills %f vs %f", refill_overhead(narrow), refill_overhead(wide));
+    EXPECT(make_plan_impl(25216, 3072, 1, 8, KAT_DTYPE_BF16, 8, 148, 1, &headline, 128, 512) ==
+                   KAT_OK &&
+               headline.cb_q > 0 && refill_overhead(headline) == 0.0,
+           "headline refills");
+  }
   // Invalid requests are refused, not planned.
   Plan p;
   EXPECT(make_plan_impl(-1, 8, 1, 1, KAT_DTYPE_F32, 0, 148, 1, &p) == KAT_ERR_BAD_SHAPE, "neg");
