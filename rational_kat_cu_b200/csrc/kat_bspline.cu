@@ -1,11 +1,12 @@
 // B-spline basis (Cox-de Boor) forward and backward for sm_100a: the basis evaluation of
 // efficient-KAN layers that the reference fuses in rational_kat_cu/bspline_basis.py.
 //
-// Work split: a block of 256 threads takes tiles of 8 batch rows x 32 features (warp w = row w,
-// lane = feature), walking the tiles of one 32-feature column before the next, so it keeps
-// those 32 features' knots in shared memory together with every clamped knot difference the
-// recursion divides by, max(t_{j+k} - t_j, 1e-8), and its correctly rounded reciprocal (per
-// feature, level k and index j).
+// Work split: a block of 256 threads takes tiles of 8 R batch rows x 32 features (warp w = rows
+// w R .. w R + R - 1, lane = feature; R = 4 or 2 for the cubic layers of grid 5 and 8, whose
+// knot count is compiled in, 1 otherwise), walking the tiles of one 32-feature column before
+// the next, so it keeps those 32 features' knots in shared memory together with every clamped
+// knot difference the recursion divides by, max(t_{j+k} - t_j, 1e-8), and its correctly rounded
+// reciprocal (per feature, level k and index j).
 //
 // Per element, instead of running the recursion over every knot interval (the reference
 // evaluates all n_knots - 1 indicators and every level in full), a thread finds the one
