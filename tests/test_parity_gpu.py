@@ -129,6 +129,14 @@ EDGE_SHAPES = [
     ((2, 32, 5, 3), 4, "nchw", "bf16"),
     ((2, 6, 1, 1), 3, "nchw", "f16"),
     ((257, 3, 96), 8, "blc", "f16"),
+    # short, wide problems: the cp.async backward takes 512-column tiles (at 128 columns more
+    # column blocks than blocks, several ring refills per block)
+    ((4, 64, 56, 56), 8, "nchw", "f32"),
+    ((4, 262144), 8, "blc", "bf16"),
+    # blocks aligned to column blocks, unevenly (16, 8 and 6 column blocks on 148 blocks)
+    ((16, 16384), 8, "blc", "bf16"),
+    ((37, 8192), 8, "blc", "bf16"),
+    ((300, 6144), 16, "blc", "f16"),
 ]
 
 
