@@ -5,7 +5,8 @@ KAT_DEVICE_BOUNDS in the device status word instead of faulting.
 
 On the edge shapes (odd and 3-wide groups, [B, C], 7x7 NCHW, several column blocks, one
 element per group, 257 rows, 12-wide groups on 8-byte vectors, misaligned pointers, empty
-input), for every dtype, both formulas and each streaming design (cp.async ring, register
+input, short and wide problems on 512-column backward tiles, blocks aligned unevenly to
+column blocks), for every dtype, both formulas and each streaming design (cp.async ring, register
 prefetch, bulk-copy ring), forward and backward through the debug build must leave the status
 word at 0 and give results bit-identical to the release build.
 """
@@ -40,6 +41,10 @@ CASES = [
     ((5, 96, 1), 4, "f32", 3),
     ((0, 768, 1), 8, "bf16", 0),          # empty input
     ((128, 3072, 1), 8, "bf16", 0),       # the headline layout, a few rows
+    ((4, 64, 3136), 8, "f32", 0),         # short, wide NCHW: 512-column backward tiles
+    ((4, 262144, 1), 8, "bf16", 0),       # short, wide [B, C]: 512-column backward tiles
+    ((37, 8192, 1), 8, "bf16", 0),        # blocks aligned to 8 column blocks, unevenly
+    ((300, 6144, 1), 16, "f16", 0),       # blocks aligned to 6 column blocks, unevenly
 ]
 CODES = {"f32": (torch.float32, _native.KAT_DTYPE_F32), "bf16": (torch.bfloat16, _native.KAT_DTYPE_BF16),
          "f16": (torch.float16, _native.KAT_DTYPE_F16)}
